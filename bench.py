@@ -1,0 +1,414 @@
+#!/usr/bin/env python3
+"""Benchmark: GCN inference (2 layers, 128 -> 128 -> 128, ReLU between layers)
+on a seeded R-MAT graph shaped like ogbn-products (2,449,029 nodes,
+61,859,140 directed entries + self-loops, symmetric normalisation), fp32.
+
+One step = one full forward over the whole graph: per layer the GCN
+aggregation (libgnnb200 SpMM), then X·W with bias and ReLU fused into the
+GEMM epilogue; with N GPUs the rows are split into N equal-nnz ranges (one
+process per GPU) and the layer-1 output rows are exchanged over NCCL.
+
+Metric: algorithmic SpMM bytes of the step (CSR + gathered neighbour rows +
+output, per layer) divided by the step time, in GB/s, whole job. The JSON line
+adds ms/layer, the SpMM kernel's roofline fraction against the measured HBM
+copy bandwidth, an end-to-end figure through the public API with host buffers
+(H2D of the inputs and D2H of the output inside the timed region), and the
+CPU oracle timed on a bounded sample on this host.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  torchrun --nproc-per-node N bench.py --gpus N ...   (N > 1)
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+from gnn_cuda_b200 import _native as N  # noqa: E402
+from gnn_cuda_b200 import partition, synth  # noqa: E402
+from gnn_cuda_b200.GNN_cuda_common import agg_ops, gcn_ops, native_ops  # noqa: E402
+
+METRIC = "SpMM GB/s & GNN fwd ms/layer at 1/2/4/8 B200; % of HBM roofline"
+WORKLOAD = "gcn_products_like"
+FEAT = 128
+LAYERS = 2
+HBM_FALLBACK_GBS = 6650.0
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--seed", type=int, default=1)
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU-baseline sample time")
+    ap.add_argument("--scale", type=float, default=1.0, help="scale the graph down (smoke runs only)")
+    return ap.parse_args()
+
+
+def measured_hbm_gbs() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        v = float(json.loads(p.read_text())["hbm_gbs"])
+        return v, "measured"
+    except Exception:
+        return HBM_FALLBACK_GBS, "fallback"
+
+
+def spmm_layer_bytes(n: int, nnz: int, f: int, rp_bytes: int = 4) -> int:
+    """Algorithmic bytes of one GCN aggregation: row_ptr + col_ind + deg_inv_sqrt
+    + one gathered feature row per CSR entry + the output matrix."""
+    return (n + 1) * rp_bytes + nnz * 4 + n * 4 + nnz * f * 4 + n * f * 4
+
+
+def profiled_traffic() -> float | None:
+    """DRAM bytes per SpMM launch from the committed ncu summary, if present."""
+    p = ROOT / "profiles" / "spmm_gcn_products_like.md"
+    if not p.exists():
+        return None
+    m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", p.read_text())
+    return float(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                                          "-lms", "100", "-i", str(self.gpu)], stdout=self.file,
+                                         stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        if self.proc is None or self.file is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        try:
+            for line in Path(self.file.name).read_text().splitlines():
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9 and parts[1].isdigit():
+                    rows.append(parts)
+            os.unlink(self.file.name)
+        except Exception:
+            pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [int(r[1]) for r in rows]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        power = []
+        for r in rows:
+            try:
+                power.append(float(r[3]))
+            except ValueError:
+                pass
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": int(rows[0][2]), "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(power) if power else None}
+
+
+# ---------------------------------------------------------------------------
+# problem construction (setup; not timed)
+# ---------------------------------------------------------------------------
+
+def build_problem(seed: int, device: torch.device, scale: float):
+    t0 = time.time()
+    src, dst, n = synth.make_graph(WORKLOAD, seed=seed, device=device, scale_nodes=scale)
+    rp, ci, dis = synth.csr_on_device(src, dst, n, add_self_loops=True)
+    del src, dst
+    x = synth.features(n, FEAT, seed=seed + 1, device=device)
+    ws = [synth.glorot(FEAT, FEAT, seed=seed + 10 + li, device=device) for li in range(LAYERS)]
+    bs = [torch.zeros(FEAT, device=device) for _ in range(LAYERS)]
+    torch.cuda.synchronize(device)
+    log(f"[bench] graph n={n} nnz={ci.numel()} built in {time.time() - t0:.1f}s")
+    return dict(n=n, rp=rp, ci=ci, dis=dis, x=x, ws=ws, bs=bs)
+
+
+def describe(prob, world: int, gemm: str | None = None) -> dict:
+    if gemm is None:
+        gemm = "tcgen05-tf32" if N.lib().gnn_gemm_uses_tensor_cores(prob["n"], FEAT, FEAT) else "ffma-fp32"
+    return {"workload": f"{WORKLOAD}: GCN {LAYERS} layers {FEAT}->{FEAT}->{FEAT}, ReLU between layers",
+            "nodes": prob["n"], "csr_entries": int(prob["ci"].numel()), "feat_dim": FEAT, "layers": LAYERS,
+            "self_loops": True, "graph": "R-MAT(0.57,0.19,0.19,0.05), symmetrised, de-duplicated",
+            "parallelism": f"rows{world}" + ("" if world == 1 else "+nccl_row_exchange"),
+            "l2": "inputs larger than L2 (X is %.2f GB), no flush" % (prob["n"] * FEAT * 4 / 1e9),
+            "gemm": gemm}
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+
+def run_ours(args, rank: int, world: int, device: torch.device):
+    prob = build_problem(args.seed, device, args.scale)
+    n = prob["n"]
+    nnz = int(prob["ci"].numel())
+    rp_cpu = prob["rp"].to(torch.int64).cpu().numpy()
+    bounds = partition.nnz_balanced_bounds(rp_cpu, world)
+    r0, r1 = bounds[rank], bounds[rank + 1]
+    shard = partition.make_shard(prob["rp"], prob["ci"], r0, r1)
+    rows = shard.num_rows
+    bufs = {"agg": torch.empty(rows, FEAT, device=device), "out0": torch.empty(rows, FEAT, device=device),
+            "out1": torch.empty(rows, FEAT, device=device)}
+    if world > 1:
+        bufs["x_next"] = torch.empty(n, FEAT, device=device)
+    torch.backends.cuda.matmul.allow_tf32 = True  # the reference driver's --tf32 default
+
+    def step(timers=None):
+        if world == 1:
+            # the reference-facing op surface, exactly what gcn_inference calls
+            x = prob["x"]
+            for li in range(LAYERS):
+                ev = partition._mark(timers, "spmm_begin")
+                gcn_ops.spmm_gcn_forward_(prob["rp"], prob["ci"], prob["dis"], x, bufs["agg"])
+                partition._mark(timers, "spmm_end", ev)
+                out = bufs["out0" if li % 2 == 0 else "out1"]
+                agg_ops.linear_forward_(bufs["agg"], prob["ws"][li], prob["bs"][li], out, li != LAYERS - 1)
+                x = out
+            return x
+        return partition.gcn_forward_partitioned(shard, prob["dis"], prob["x"], prob["ws"], prob["bs"], bounds, rank,
+                                                 bufs, timers=timers)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(device)
+
+    timers: dict = {}
+    launches0 = N.lib().gnn_kernel_launches()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device.index) as clocks:
+        t_start.record()
+        for _ in range(args.steps):
+            step(timers)
+        t_end.record()
+        torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    launches = N.lib().gnn_kernel_launches() - launches0
+    ms_total = t_start.elapsed_time(t_end)
+    spmm_ms = [b.elapsed_time(e) for b, e in timers.get("spmm", [])]
+    spmm_ms_avg = sum(spmm_ms) / max(1, len(spmm_ms))
+
+    # ---- e2e through the public API with host buffers ----
+    # every step copies this rank's inputs (its CSR rows, the normalisation vector,
+    # the full feature matrix, the weights) from pinned host memory, runs the
+    # forward and reads its output rows back into pinned host memory.
+    if world == 1:
+        dev_in = [prob["rp"], prob["ci"], prob["dis"], prob["x"]]
+    else:
+        dev_in = [shard.row_ptr, shard.col_ind, prob["dis"], prob["x"]]
+    dev_in += prob["ws"] + prob["bs"]
+    host_in = [t.cpu().pin_memory() for t in dev_in]
+    out_host = torch.empty(rows, FEAT, pin_memory=True)
+    h2d = sum(t.numel() * t.element_size() for t in host_in)
+    d2h = out_host.numel() * 4
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    e_start = torch.cuda.Event(enable_timing=True)
+    e_end = torch.cuda.Event(enable_timing=True)
+    e_start.record()
+    for _ in range(args.e2e_steps):
+        for dst_t, src_t in zip(dev_in, host_in):
+            dst_t.copy_(src_t, non_blocking=True)
+        out = step()
+        out_host.copy_(out, non_blocking=True)
+    e_end.record()
+    torch.cuda.synchronize(device)
+    e2e_ms = e_start.elapsed_time(e_end)
+
+    # ---- reduce over ranks ----
+    vals = torch.tensor([ms_total, e2e_ms, spmm_ms_avg, float(launches)], dtype=torch.float64, device=device)
+    if world > 1:
+        mx = vals.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        sm = vals.clone()
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+        ms_total, e2e_ms, spmm_ms_avg = float(mx[0]), float(mx[1]), float(mx[2])
+        launches = int(sm[3])
+    bytes_layer = spmm_layer_bytes(n, nnz, FEAT)
+    bytes_step = bytes_layer * LAYERS
+    ms_step = ms_total / args.steps
+    value = bytes_step / (ms_step * 1e-3) / 1e9
+    e2e_value = bytes_step / ((e2e_ms / args.e2e_steps) * 1e-3) / 1e9
+
+    if rank != 0:
+        return None
+    peak, peak_kind = measured_hbm_gbs()
+    # per-launch algorithmic bytes of the dominant kernel on one GPU (its shard)
+    shard_bytes = spmm_layer_bytes(rows, shard.num_edges, FEAT)
+    achieved = shard_bytes / (spmm_ms_avg * 1e-3) / 1e9 if spmm_ms_avg > 0 else None
+    traffic = profiled_traffic()
+    result = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "ms_per_layer": round(ms_step / LAYERS, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
+        "data": f"synthetic: seeded R-MAT graph (seed {args.seed}) with ogbn-products shape, N(0,1) features, "
+                "Glorot weights, zero bias",
+        "config": describe(prob, world),
+        "roofline": {"bound": "hbm", "kernel": "spmm_vec_kernel (GCN aggregation)",
+                     "achieved": round(achieved, 1) if achieved else None, "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4) if achieved else None, "peak_source": peak_kind,
+                     "spmm_ms_per_launch": round(spmm_ms_avg, 4), "algorithmic_bytes_per_launch": shard_bytes,
+                     "traffic": traffic},
+        "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
+                "d2h_bytes_per_step": int(d2h), "ms_per_step": round(e2e_ms / args.e2e_steps, 3),
+                "api": "gnn_cuda_b200.GNN_cuda_common.gcn_ops/agg_ops over libgnnb200.so"},
+        "gpu_launches": int(launches),
+        "clocks": clocks.summary(),
+    }
+    if world == 1:
+        result["cpu_baseline"] = cpu_baseline(prob, args.cpu_seconds)
+    return result
+
+
+# ---------------------------------------------------------------------------
+# CPU oracle (baseline leg of our arm, and the whole --impl reference arm)
+# ---------------------------------------------------------------------------
+
+def _host_problem(prob):
+    return dict(n=prob["n"], rp=prob["rp"].cpu().numpy(), ci=prob["ci"].cpu().numpy(),
+                dis=prob["dis"].cpu().numpy(), x=prob["x"].cpu().numpy(),
+                ws=[w.cpu().numpy() for w in prob["ws"]], bs=[b.cpu().numpy() for b in prob["bs"]])
+
+
+def _cpu_rows_layer(O, hp, r0: int, r1: int, threads: int):
+    """One GCN layer (aggregation + X·W + bias + ReLU) on rows [r0, r1) with the oracle."""
+    agg = O.spmm(hp["rp"], hp["ci"], hp["x"], mode=O.W_GCN, dis=hp["dis"], rows=(r0, r1), nthreads=threads)
+    return O.gemm_fp32(agg, hp["ws"][0], hp["bs"][0], True, nthreads=threads)
+
+
+def _cpu_sample_rows(O, hp, seconds: float, threads: int) -> tuple[int, float]:
+    n = hp["n"]
+    probe = max(1, n // 512)
+    t0 = time.perf_counter()
+    _cpu_rows_layer(O, hp, 0, probe, threads)
+    dt = max(time.perf_counter() - t0, 1e-4)
+    rows = int(min(n, max(probe, probe * seconds / dt)))
+    return rows, dt
+
+
+def _sample_bytes(hp, rows: int) -> int:
+    nnz = int(hp["rp"][rows]) - int(hp["rp"][0])
+    return spmm_layer_bytes(rows, nnz, FEAT)
+
+
+def cpu_baseline(prob, seconds: float) -> dict:
+    from oracle import oracle as O
+    hp = _host_problem(prob)
+    threads = O.max_threads()
+    _cpu_rows_layer(O, hp, 0, 1, threads)  # warm the oracle library and page in the inputs
+    rows, _ = _cpu_sample_rows(O, hp, seconds, threads)
+    t0 = time.perf_counter()
+    _cpu_rows_layer(O, hp, 0, rows, threads)
+    dt = time.perf_counter() - t0
+    return {"value": round(_sample_bytes(hp, rows) / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"one GCN layer (aggregation + X·W + bias + ReLU) on rows [0, {rows}) of {hp['n']} "
+                      f"({_sample_bytes(hp, rows) / 1e9:.2f} algorithmic GB) in {dt:.2f} s; C oracle, OpenMP"}
+
+
+def run_reference(args, device: torch.device):
+    from oracle import oracle as O
+    prob = build_problem(args.seed, device, args.scale)
+    hp = _host_problem(prob)
+    cfg = describe(prob, args.gpus, gemm="cpu-fp32")
+    del prob
+    torch.cuda.empty_cache()
+    threads = O.max_threads()
+    total = args.steps + args.warmup
+    per_step = max(0.5, min(4.0, 150.0 / max(1, total)))  # whole run within a few minutes
+    rows, _ = _cpu_sample_rows(O, hp, per_step, threads)
+    for _ in range(args.warmup):
+        _cpu_rows_layer(O, hp, 0, rows, threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        _cpu_rows_layer(O, hp, 0, rows, threads)
+    dt = time.perf_counter() - t0
+    value = _sample_bytes(hp, rows) * args.steps / dt / 1e9
+    sample = (f"each step: one GCN layer (aggregation + X·W + bias + ReLU) on rows [0, {rows}) of {hp['n']} "
+              f"({_sample_bytes(hp, rows) / 1e9:.2f} algorithmic GB); C restatement of the reference arithmetic, "
+              f"OpenMP over rows")
+    return {"metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "fp32", "impl": "reference",
+            "data": f"synthetic: seeded R-MAT graph (seed {args.seed}) with ogbn-products shape",
+            "config": cfg,
+            "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main() -> int:
+    args = parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        log(f"[bench] WORLD_SIZE={world} but --gpus={args.gpus}; using WORLD_SIZE")
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        print(json.dumps(run_reference(args, device)), flush=True)
+        return 0
+    if world > 1:
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)
+    try:
+        res = run_ours(args, rank, world, device)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -1,0 +1,170 @@
+"""CSR construction for the aggregation kernels (reference: GNN_cuda_common/graph_utils.py).
+
+The CSR contract is the reference's and is reproduced bit for bit:
+  * rows are destinations (incoming edges) unless ``transpose_for_incoming``
+    is False; columns are sources;
+  * self-loops are appended when asked (an existing loop merges with the new one);
+  * duplicate (row, col) pairs collapse to one entry and columns are sorted
+    within a row (scipy's ``tocsr()`` + ``sort_indices()`` in the reference);
+  * ``deg_inv_sqrt = clip(deg, 1)^-0.5`` evaluated in float32 by numpy's power,
+    and PyG edge weights ``dis[row] * dis[col]`` in float32;
+  * ``row_ptr`` / ``col_ind`` are int32.
+The construction here is a single sort of 64-bit (row, col) keys instead of a
+sparse-matrix library conversion. Deviation, on purpose: where the reference's
+int32 cast would silently wrap (more than 2^31-1 entries), ``index_dtype``
+int32 raises, and ``index_dtype=torch.int64`` returns an int64 ``row_ptr``.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from pathlib import Path
+
+import numpy as np
+import torch
+
+
+@dataclass
+class NormalizedCSR:
+    row_ptr: torch.Tensor
+    col_ind: torch.Tensor
+    deg_inv_sqrt: torch.Tensor
+    num_nodes: int
+    num_edges: int
+
+
+@dataclass
+class PlainCSR:
+    row_ptr: torch.Tensor
+    col_ind: torch.Tensor
+    num_nodes: int
+    num_edges: int
+
+
+@dataclass
+class WeightedCSR:
+    row_ptr: torch.Tensor
+    col_ind: torch.Tensor
+    edge_weight: torch.Tensor
+    num_nodes: int
+    num_edges: int
+
+
+def default_gcn_preprocess_meta_path(dataset: str, *, data_root: str) -> str:
+    return str(Path(data_root) / "gnn_cuda_preprocessed" / "gcn" / f"{dataset}.pt")
+
+
+def feature_rows_per_page(*, feat_dim: int, page_bytes: int = 4096, dtype_bytes: int = 4) -> int:
+    row_bytes = max(1, int(feat_dim) * int(dtype_bytes))
+    return max(1, int(page_bytes) // row_bytes)
+
+
+def apply_node_permutation(src, dst, features, *, perm, inv_perm):
+    """Relabel nodes: new id of old node v is inv_perm[v]; feature row i of the
+    result is old row perm[i]."""
+    inv = torch.as_tensor(inv_perm).to(dtype=torch.long, device="cpu").contiguous()
+    p = torch.as_tensor(perm).to(dtype=torch.long, device="cpu").contiguous()
+    return inv[src.long().cpu()].contiguous(), inv[dst.long().cpu()].contiguous(), features[p].contiguous()
+
+
+def apply_graph_permutation(src, dst, *, inv_perm):
+    inv = torch.as_tensor(inv_perm).to(dtype=torch.long, device="cpu").contiguous()
+    return inv[src.long().cpu()].contiguous(), inv[dst.long().cpu()].contiguous()
+
+
+def _as_np(t) -> np.ndarray:
+    if isinstance(t, torch.Tensor):
+        return t.detach().cpu().numpy().astype(np.int64, copy=False)
+    return np.asarray(t, dtype=np.int64)
+
+
+def csr_from_pairs(rows: np.ndarray, cols: np.ndarray, num_nodes: int) -> tuple[np.ndarray, np.ndarray]:
+    """Sorted, de-duplicated CSR (int64 row_ptr, int64 col) of (row, col) pairs."""
+    n = int(num_nodes)
+    rows = np.asarray(rows, dtype=np.int64)
+    cols = np.asarray(cols, dtype=np.int64)
+    if rows.size:
+        if rows.min() < 0:
+            raise ValueError("negative row index found")
+        if cols.min() < 0:
+            raise ValueError("negative column index found")
+        if rows.max() >= n:
+            raise ValueError("row index exceeds matrix dimensions")
+        if cols.max() >= n:
+            raise ValueError("column index exceeds matrix dimensions")
+    keys = np.unique(rows * np.int64(n) + cols) if rows.size else np.zeros(0, np.int64)
+    r = keys // np.int64(max(n, 1))
+    c = keys - r * np.int64(n)
+    row_ptr = np.zeros(n + 1, dtype=np.int64)
+    if n:
+        np.cumsum(np.bincount(r, minlength=n), out=row_ptr[1:])
+    return row_ptr, c
+
+
+def _pairs(src, dst, num_nodes: int, add_self_loops: bool, dst_major: bool):
+    s, d = _as_np(src), _as_np(dst)
+    if add_self_loops:
+        loop = np.arange(int(num_nodes), dtype=np.int64)
+        s, d = np.concatenate([s, loop]), np.concatenate([d, loop])
+    return (d, s) if dst_major else (s, d)
+
+
+def _index(a: np.ndarray, dtype: torch.dtype, what: str) -> torch.Tensor:
+    if dtype == torch.int32:
+        if a.size and int(a.max()) > np.iinfo(np.int32).max:
+            raise ValueError(f"{what} exceeds int32 range; pass index_dtype=torch.int64")
+        return torch.from_numpy(a.astype(np.int32)).contiguous()
+    return torch.from_numpy(a.astype(np.int64)).contiguous()
+
+
+def deg_inv_sqrt_of(row_ptr: np.ndarray) -> np.ndarray:
+    """float32 clip(deg, 1)^-0.5 through numpy's float32 power (the normalisation
+    must be this exact float32 function to match the reference bit for bit)."""
+    deg = np.diff(np.asarray(row_ptr, dtype=np.int64)).astype(np.float32)
+    return np.power(np.clip(deg, np.float32(1.0), None), np.float32(-0.5)).astype(np.float32)
+
+
+def build_gcn_normalized_csr(src, dst, *, num_nodes: int, add_self_loops: bool = True,
+                             index_dtype: torch.dtype = torch.int32) -> NormalizedCSR:
+    r, c = _pairs(src, dst, num_nodes, add_self_loops, dst_major=True)
+    row_ptr, col = csr_from_pairs(r, c, num_nodes)
+    return NormalizedCSR(row_ptr=_index(row_ptr, index_dtype, "row_ptr"), col_ind=_index(col, torch.int32, "col_ind"),
+                         deg_inv_sqrt=torch.from_numpy(deg_inv_sqrt_of(row_ptr)).contiguous(),
+                         num_nodes=int(num_nodes), num_edges=int(col.shape[0]))
+
+
+def build_pyg_gcn_weighted_csr(src, dst, *, num_nodes: int, add_self_loops: bool = True,
+                               index_dtype: torch.dtype = torch.int32) -> WeightedCSR:
+    r, c = _pairs(src, dst, num_nodes, add_self_loops, dst_major=True)
+    row_ptr, col = csr_from_pairs(r, c, num_nodes)
+    dis = deg_inv_sqrt_of(row_ptr)
+    row_of_edge = np.repeat(np.arange(int(num_nodes), dtype=np.int64), np.diff(row_ptr))
+    ew = (dis[row_of_edge] * dis[col]).astype(np.float32)
+    return WeightedCSR(row_ptr=_index(row_ptr, index_dtype, "row_ptr"), col_ind=_index(col, torch.int32, "col_ind"),
+                       edge_weight=torch.from_numpy(ew).contiguous(), num_nodes=int(num_nodes),
+                       num_edges=int(col.shape[0]))
+
+
+def build_plain_csr(src, dst, *, num_nodes: int, add_self_loops: bool = False, transpose_for_incoming: bool = True,
+                    index_dtype: torch.dtype = torch.int32) -> PlainCSR:
+    r, c = _pairs(src, dst, num_nodes, add_self_loops, dst_major=transpose_for_incoming)
+    row_ptr, col = csr_from_pairs(r, c, num_nodes)
+    return PlainCSR(row_ptr=_index(row_ptr, index_dtype, "row_ptr"), col_ind=_index(col, torch.int32, "col_ind"),
+                    num_nodes=int(num_nodes), num_edges=int(col.shape[0]))
+
+
+def load_src_dst_features(loaded, *, load_kind: str):
+    if load_kind == "pyg":
+        edge_index, features, num_nodes = loaded
+        return edge_index[0].contiguous(), edge_index[1].contiguous(), features, num_nodes
+    if load_kind == "dgl":
+        src, dst, features, num_nodes = loaded
+        return src.contiguous(), dst.contiguous(), features, num_nodes
+    raise ValueError(f"Unsupported load_kind: {load_kind}")
+
+
+def resolve_dataset_path(dataset: str, *, data_root: str) -> str:
+    if dataset == "all":
+        raise ValueError("'all' is only supported by the run/ entrypoints")
+    if "/" in dataset or "\\" in dataset or dataset.endswith(".npz"):
+        raise ValueError("--dataset only accepts a dataset name or 'all'")
+    return str(Path(data_root) / f"{dataset}.npz")

@@ -1,0 +1,94 @@
+// Shared internals of libgnnb200.so: status/error plumbing, tuning knobs and
+// small device helpers. Nothing here is part of the public C ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <atomic>
+#include <string>
+
+#include "../../include/gnn_b200.h"
+
+namespace gnnb200 {
+
+// ---- error reporting ---------------------------------------------------------
+void set_error(const std::string& msg);
+void clear_error();
+
+// Returns `status` after recording `msg` as the thread's last error.
+inline int fail(int status, const std::string& msg) {
+  set_error(msg);
+  return status;
+}
+
+// Checks the result of a CUDA runtime call; on failure records
+// "<what>: <cuda error string>" and returns GNN_ERR_CUDA from the caller.
+#define GNN_CUDA_TRY(expr, what)                                                   \
+  do {                                                                             \
+    cudaError_t err__ = (expr);                                                    \
+    if (err__ != cudaSuccess) {                                                    \
+      return ::gnnb200::fail(GNN_ERR_CUDA, std::string(what) + ": " +              \
+                                               cudaGetErrorString(err__));         \
+    }                                                                              \
+  } while (0)
+
+// Process-wide count of kernels launched by this library.
+void count_launch();
+
+// After a kernel launch: surfaces launch-configuration errors immediately, as
+// the reference does with C10_CUDA_CHECK(cudaGetLastError()), and counts it.
+#define GNN_LAUNCH_CHECK(what)                 \
+  do {                                         \
+    GNN_CUDA_TRY(cudaGetLastError(), what);    \
+    ::gnnb200::count_launch();                 \
+  } while (0)
+
+#define GNN_REQUIRE(cond, status, msg)   \
+  do {                                   \
+    if (!(cond)) {                       \
+      return ::gnnb200::fail(status, msg); \
+    }                                    \
+  } while (0)
+
+// ---- tuning knobs ---------------------------------------------------------------
+struct Config {
+  std::atomic<int64_t> long_row_threshold{0};  // 0 = automatic
+  std::atomic<int64_t> long_row_warps{16};
+};
+Config& config();
+
+// Number of SMs of the current device (cached per device).
+int sm_count();
+
+// ---- device helpers ---------------------------------------------------------------
+__device__ __forceinline__ float4 ldg_f4(const float4* p) { return __ldg(p); }
+
+// Streaming (read-once) loads for index/weight arrays: do not keep them in L1.
+__device__ __forceinline__ int ld_stream_i32(const int32_t* p) {
+  int v;
+  asm volatile("ld.global.nc.L1::no_allocate.b32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ float ld_stream_f32(const float* p) {
+  float v;
+  asm volatile("ld.global.nc.L1::no_allocate.f32 %0, [%1];" : "=f"(v) : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ float4 fma4(float w, float4 v, float4 acc) {
+  acc.x = __fmaf_rn(w, v.x, acc.x);
+  acc.y = __fmaf_rn(w, v.y, acc.y);
+  acc.z = __fmaf_rn(w, v.z, acc.z);
+  acc.w = __fmaf_rn(w, v.w, acc.w);
+  return acc;
+}
+__device__ __forceinline__ float4 add4(float4 a, float4 b) {
+  a.x = __fadd_rn(a.x, b.x);
+  a.y = __fadd_rn(a.y, b.y);
+  a.z = __fadd_rn(a.z, b.z);
+  a.w = __fadd_rn(a.w, b.w);
+  return a;
+}
+
+}  // namespace gnnb200

@@ -1,0 +1,668 @@
+// CSR aggregation (SpMM) engine for GCN / PyG-weighted GCN / sum / mean.
+//
+// One engine serves every aggregation entry point of the reference
+// (GNN_cuda_common/native/gcn_ops.cu:16-194, pyg_gcn_ops.cu:16-192,
+// agg_ops.cu:23-130). The per-edge arithmetic is the reference's:
+//   GCN     acc = fma(dis[r] * dis[c], x[c], acc)      (gcn_ops.cu:68-75)
+//   PyG     acc = fma(edge_weight[e], x[c], acc)       (pyg_gcn_ops.cu:71-74)
+//   sum     acc = acc + x[c]                           (agg_ops.cu:83-86)
+//   mean    sum, then acc / deg or acc * (1 / deg)     (agg_ops.cu:40-45, :102-111)
+// accumulated edge by edge in CSR order, so rows handled by a single warp give
+// the same bits as the reference kernels.
+//
+// B200 mapping
+//   * Normal rows: one warp per row. Each pass over a 32-edge chunk loads the 32
+//     column indices (and weights) with one coalesced streaming load, then the
+//     warp gathers U neighbour rows at a time with 128-bit loads (lane l owns
+//     float4 columns l, l+32, ...), so U x 512 B per warp are in flight before
+//     the first FMA. Output rows are written with one coalesced 128-bit store
+//     per lane.
+//   * Long rows (degree > threshold, the power-law hubs): a per-call plan
+//     kernel lists them in the caller's workspace; the first CTAs of the main
+//     grid pull them from that list with an atomic ticket and split each one
+//     into contiguous per-warp edge ranges. The warp partials are added in warp
+//     order through shared memory: deterministic, no float atomics.
+//   * Feature widths that are not a multiple of 4 (or unaligned bases) use a
+//     scalar warp-per-row kernel in plain CSR order.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <algorithm>
+#include <string>
+
+#include "common.cuh"
+
+namespace gnnb200 {
+namespace {
+
+constexpr unsigned kFull = 0xffffffffu;
+constexpr int kBlockThreads = 512;       // 16 warps
+constexpr int kRowsPerWarp = 4;          // rows a warp takes per normal block
+constexpr int kTileF4 = 128;             // float4 columns per feature tile (512 floats)
+constexpr int kMaxTiles = 62;            // per-tile tickets live in the workspace header
+constexpr size_t kWsHeader = 256;        // counters: [0] long-row count, [2+t] ticket of tile t
+constexpr int64_t kMinLongThreshold = 32;
+
+enum WeightMode : int { kUnit = 0, kGcn = 1, kEdge = 2 };
+enum MeanMode : int { kNoMean = 0, kMeanDiv = 1, kMeanRcp = 2 };
+
+struct SpmmArgs {
+  const void* row_ptr;
+  const int32_t* col;
+  const float* dis;        // GCN normalisation vector, indexed by (global) column id
+  const float* dis_row;    // GCN row scale base: dis_row[r] for local row r
+  const float* ew;         // PyG edge weights
+  const float* x;
+  const float* hot;        // optimized mode: device copy of rows [0, hot_cutoff)
+  int64_t hot_cutoff;
+  const int64_t* sched;    // optional row schedule (slot -> row)
+  float* out;
+  int64_t n;
+  int64_t f;
+  int64_t long_thr;
+  uint32_t* counters;
+  uint32_t* long_list;
+  int64_t long_cap;
+};
+
+template <int WM>
+__device__ __forceinline__ float edge_weight(const SpmmArgs& a, float rs, int c, int64_t e) {
+  if constexpr (WM == kGcn) {
+    return __fmul_rn(rs, __ldg(a.dis + c));
+  } else if constexpr (WM == kEdge) {
+    return ld_stream_f32(a.ew + e);
+  } else {
+    return 1.0f;
+  }
+}
+
+template <bool HOT>
+__device__ __forceinline__ const float* feature_row(const SpmmArgs& a, int c) {
+  if constexpr (HOT) {
+    if (c < a.hot_cutoff) return a.hot + static_cast<int64_t>(c) * a.f;
+  }
+  return a.x + static_cast<int64_t>(c) * a.f;
+}
+
+// Accumulates edges [beg, end) of one row into acc, edge by edge in CSR order.
+// All 32 lanes of the warp must call this with the same arguments.
+template <int WM, bool HOT, int NV, int U, class IdxT>
+__device__ __forceinline__ void accumulate_edges(const SpmmArgs& a, IdxT beg, IdxT end, float rs,
+                                                 int lane, int64_t col0, const bool (&valid)[NV],
+                                                 float4 (&acc)[NV]) {
+  static_assert(32 % U == 0, "U must divide the warp size");
+  for (IdxT base = beg; base < end; base += 32) {
+    const int cnt = static_cast<int>(min(static_cast<IdxT>(32), static_cast<IdxT>(end - base)));
+    int c = 0;
+    float w = 0.0f;
+    if (lane < cnt) {
+      c = ld_stream_i32(a.col + base + lane);
+      w = edge_weight<WM>(a, rs, c, static_cast<int64_t>(base) + lane);
+    }
+    for (int j = 0; j < cnt; j += U) {
+      float4 v[U][NV];
+#pragma unroll
+      for (int k = 0; k < U; ++k) {
+        const int ck = __shfl_sync(kFull, c, j + k);
+        if (j + k < cnt) {
+          const float4* row = reinterpret_cast<const float4*>(feature_row<HOT>(a, ck));
+#pragma unroll
+          for (int q = 0; q < NV; ++q) {
+            if (valid[q]) v[k][q] = ldg_f4(row + col0 + 32 * q);
+          }
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < U; ++k) {
+        const float wk = __shfl_sync(kFull, w, j + k);
+        if (j + k < cnt) {
+#pragma unroll
+          for (int q = 0; q < NV; ++q) {
+            if (valid[q]) {
+              if constexpr (WM == kUnit) {
+                acc[q] = add4(acc[q], v[k][q]);
+              } else {
+                acc[q] = fma4(wk, v[k][q], acc[q]);
+              }
+            }
+          }
+        }
+      }
+    }
+  }
+}
+
+template <int MEAN>
+__device__ __forceinline__ float4 finish(float4 acc, int64_t deg) {
+  if constexpr (MEAN == kMeanDiv) {
+    if (deg > 0) {
+      const float d = static_cast<float>(deg);
+      acc.x = __fdiv_rn(acc.x, d);
+      acc.y = __fdiv_rn(acc.y, d);
+      acc.z = __fdiv_rn(acc.z, d);
+      acc.w = __fdiv_rn(acc.w, d);
+    }
+  } else if constexpr (MEAN == kMeanRcp) {
+    if (deg > 0) {
+      const float inv = __fdiv_rn(1.0f, static_cast<float>(deg));
+      acc.x = __fmul_rn(acc.x, inv);
+      acc.y = __fmul_rn(acc.y, inv);
+      acc.z = __fmul_rn(acc.z, inv);
+      acc.w = __fmul_rn(acc.w, inv);
+    }
+  }
+  return acc;
+}
+
+// Lists the rows whose degree exceeds the long-row threshold.
+template <class IdxT>
+__global__ void plan_long_rows_kernel(const IdxT* __restrict__ row_ptr, int64_t n, int64_t thr,
+                                      uint32_t* __restrict__ counters,
+                                      uint32_t* __restrict__ list, int64_t cap) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; r < n;
+       r += stride) {
+    const int64_t deg = static_cast<int64_t>(row_ptr[r + 1]) - static_cast<int64_t>(row_ptr[r]);
+    if (deg > thr) {
+      const uint32_t i = atomicAdd(&counters[0], 1u);
+      if (i < cap) list[i] = static_cast<uint32_t>(r);
+    }
+  }
+}
+
+// Main vector kernel. Blocks [0, num_long_blocks) serve the long-row list;
+// the rest take kRowsPerWarp rows per warp, skipping long rows.
+template <int WM, int MEAN, bool HOT, int NV, class IdxT>
+__global__ void __launch_bounds__(kBlockThreads, 2)
+    spmm_vec_kernel(SpmmArgs a, int num_long_blocks) {
+  constexpr int U = (NV == 1) ? 8 : (NV == 2 ? 4 : 2);
+  extern __shared__ float4 s_part[];  // [nwarps][32 * NV] (long rows only)
+  __shared__ uint32_t s_ticket;
+
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int nwarps = blockDim.x >> 5;
+  const int tile = blockIdx.y;
+  const int64_t f4 = a.f >> 2;
+  const int64_t col0 = static_cast<int64_t>(tile) * kTileF4 + lane;
+  bool valid[NV];
+#pragma unroll
+  for (int q = 0; q < NV; ++q) valid[q] = (col0 + 32 * q) < f4;
+  const IdxT* __restrict__ rp = static_cast<const IdxT*>(a.row_ptr);
+
+  if (static_cast<int>(blockIdx.x) < num_long_blocks) {
+    // ---- long rows: one row per CTA iteration, split across all warps ----
+    const uint32_t count = min(__ldcg(&a.counters[0]), static_cast<uint32_t>(a.long_cap));
+    while (true) {
+      if (threadIdx.x == 0) s_ticket = atomicAdd(&a.counters[2 + tile], 1u);
+      __syncthreads();
+      const uint32_t t = s_ticket;
+      if (t >= count) break;
+      const int64_t r = a.long_list[t];
+      const IdxT beg = rp[r];
+      const IdxT end = rp[r + 1];
+      const int64_t deg = static_cast<int64_t>(end - beg);
+      const int64_t chunk = (deg + nwarps - 1) / nwarps;
+      const IdxT wb = static_cast<IdxT>(min(static_cast<int64_t>(beg) + warp * chunk, static_cast<int64_t>(end)));
+      const IdxT we = static_cast<IdxT>(min(static_cast<int64_t>(wb) + chunk, static_cast<int64_t>(end)));
+        const float rs = (WM == kGcn) ? __ldg(a.dis_row + r) : 1.0f;
+      float4 acc[NV];
+#pragma unroll
+      for (int q = 0; q < NV; ++q) acc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+      accumulate_edges<WM, HOT, NV, U, IdxT>(a, wb, we, rs, lane, col0, valid, acc);
+#pragma unroll
+      for (int q = 0; q < NV; ++q) s_part[warp * 32 * NV + q * 32 + lane] = acc[q];
+      __syncthreads();
+      // fixed-order reduction over warps: ((p0 + p1) + p2) + ...
+      for (int j = threadIdx.x; j < 32 * NV; j += blockDim.x) {
+        const int64_t cj = static_cast<int64_t>(tile) * kTileF4 + j;  // float4 column
+        if (cj < f4) {
+          float4 s = s_part[j];
+          for (int w = 1; w < nwarps; ++w) s = add4(s, s_part[w * 32 * NV + j]);
+          s = finish<MEAN>(s, deg);
+          reinterpret_cast<float4*>(a.out + r * a.f)[cj] = s;
+        }
+      }
+      __syncthreads();
+    }
+    return;
+  }
+
+  // ---- normal rows ----
+  const int64_t blk = static_cast<int64_t>(blockIdx.x) - num_long_blocks;
+  for (int i = 0; i < kRowsPerWarp; ++i) {
+    const int64_t slot = (blk * kRowsPerWarp + i) * nwarps + warp;
+    if (slot >= a.n) break;
+    const int64_t r = a.sched ? a.sched[slot] : slot;
+    const IdxT beg = rp[r];
+    const IdxT end = rp[r + 1];
+    const int64_t deg = static_cast<int64_t>(end - beg);
+    if (deg > a.long_thr) continue;  // owned by a long-row CTA
+    const float rs = (WM == kGcn) ? __ldg(a.dis_row + r) : 1.0f;
+    float4 acc[NV];
+#pragma unroll
+    for (int q = 0; q < NV; ++q) acc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+    accumulate_edges<WM, HOT, NV, U, IdxT>(a, beg, end, rs, lane, col0, valid, acc);
+    float4* orow = reinterpret_cast<float4*>(a.out + r * a.f);
+#pragma unroll
+    for (int q = 0; q < NV; ++q) {
+      if (valid[q]) orow[col0 + 32 * q] = finish<MEAN>(acc[q], deg);
+    }
+  }
+}
+
+// Scalar kernel for feature widths that are not a multiple of 4 (or unaligned
+// pointers): one warp per row, lane l owns features l, l+32, l+64, l+96 of the
+// block's 128-feature tile; plain CSR order for every row.
+template <int WM, int MEAN, bool HOT, class IdxT>
+__global__ void __launch_bounds__(256) spmm_scalar_kernel(SpmmArgs a) {
+  constexpr int SV = 4;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int nwarps = blockDim.x >> 5;
+  const int64_t fbase = static_cast<int64_t>(blockIdx.y) * 32 * SV + lane;
+  const IdxT* __restrict__ rp = static_cast<const IdxT*>(a.row_ptr);
+  const int64_t slot = static_cast<int64_t>(blockIdx.x) * nwarps + warp;
+  if (slot >= a.n) return;
+  const int64_t r = a.sched ? a.sched[slot] : slot;
+  const IdxT beg = rp[r];
+  const IdxT end = rp[r + 1];
+  const float rs = (WM == kGcn) ? __ldg(a.dis_row + r) : 1.0f;
+  float acc[SV] = {0.f, 0.f, 0.f, 0.f};
+  for (IdxT base = beg; base < end; base += 32) {
+    const int cnt = static_cast<int>(min(static_cast<IdxT>(32), static_cast<IdxT>(end - base)));
+    int c = 0;
+    float w = 0.0f;
+    if (lane < cnt) {
+      c = ld_stream_i32(a.col + base + lane);
+      w = edge_weight<WM>(a, rs, c, static_cast<int64_t>(base) + lane);
+    }
+    for (int j = 0; j < cnt; ++j) {
+      const int cj = __shfl_sync(kFull, c, j);
+      const float wj = __shfl_sync(kFull, w, j);
+      const float* row = feature_row<HOT>(a, cj);
+#pragma unroll
+      for (int s = 0; s < SV; ++s) {
+        const int64_t fi = fbase + 32 * s;
+        if (fi < a.f) {
+          const float v = __ldg(row + fi);
+          acc[s] = (WM == kUnit) ? __fadd_rn(acc[s], v) : __fmaf_rn(wj, v, acc[s]);
+        }
+      }
+    }
+  }
+  const int64_t deg = static_cast<int64_t>(end - beg);
+#pragma unroll
+  for (int s = 0; s < SV; ++s) {
+    const int64_t fi = fbase + 32 * s;
+    if (fi < a.f) {
+      float v = acc[s];
+      if (MEAN == kMeanDiv && deg > 0) v = __fdiv_rn(v, static_cast<float>(deg));
+      if (MEAN == kMeanRcp && deg > 0) v = __fmul_rn(v, __fdiv_rn(1.0f, static_cast<float>(deg)));
+      a.out[r * a.f + fi] = v;
+    }
+  }
+}
+
+int64_t long_capacity(int64_t n, int64_t nnz) {
+  return std::max<int64_t>(0, std::min<int64_t>(n, nnz / (kMinLongThreshold + 1) + 1));
+}
+
+int64_t resolve_long_threshold(int64_t n, int64_t nnz) {
+  int64_t thr = config().long_row_threshold.load();
+  if (thr <= 0) {
+    // A row is "long" when one warp would spend more than ~1/8 of the average
+    // per-warp share of the whole launch on it (148 SMs x 32 resident warps).
+    const int64_t warps = static_cast<int64_t>(sm_count()) * 32;
+    thr = nnz / std::max<int64_t>(1, warps * 8);
+    thr = std::min<int64_t>(8192, std::max<int64_t>(256, thr));
+  }
+  return std::max(thr, kMinLongThreshold);
+}
+
+template <int WM, int MEAN, bool HOT, class IdxT>
+int launch_vec(SpmmArgs a, cudaStream_t stream) {
+  const int64_t f4 = a.f >> 2;
+  const int64_t tiles = (f4 + kTileF4 - 1) / kTileF4;
+  const int64_t lanes_f4 = std::min<int64_t>(f4, kTileF4);
+  const int nv = static_cast<int>((lanes_f4 + 31) / 32);
+  const int nwarps = static_cast<int>(config().long_row_warps.load());
+  const int threads = nwarps * 32;
+  const int64_t rows_per_block = static_cast<int64_t>(nwarps) * kRowsPerWarp;
+  const int64_t normal_blocks = (a.n + rows_per_block - 1) / rows_per_block;
+
+  int num_long_blocks = 0;
+  if (a.long_cap > 0 && a.counters != nullptr) {
+    num_long_blocks = static_cast<int>(std::min<int64_t>(a.long_cap, 2 * sm_count()));
+  }
+  const int64_t gx = normal_blocks + num_long_blocks;
+  if (gx > 0x7fffffffLL) return fail(GNN_ERR_UNSUPPORTED, "spmm: too many rows for one launch");
+  dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(tiles));
+  dim3 block(threads);
+  const size_t smem = static_cast<size_t>(nwarps) * 32 * nv * sizeof(float4);
+
+#define GNN_LAUNCH_NV(NVV)                                                                   \
+  spmm_vec_kernel<WM, MEAN, HOT, NVV, IdxT><<<grid, block, smem, stream>>>(a, num_long_blocks)
+  switch (nv) {
+    case 1: GNN_LAUNCH_NV(1); break;
+    case 2: GNN_LAUNCH_NV(2); break;
+    case 3: GNN_LAUNCH_NV(3); break;
+    default: GNN_LAUNCH_NV(4); break;
+  }
+#undef GNN_LAUNCH_NV
+  GNN_LAUNCH_CHECK("spmm kernel launch");
+  return GNN_OK;
+}
+
+template <int WM, int MEAN, bool HOT, class IdxT>
+int launch_scalar(SpmmArgs a, cudaStream_t stream) {
+  const int threads = 256;
+  const int64_t rows_per_block = threads / 32;
+  const int64_t gx = (a.n + rows_per_block - 1) / rows_per_block;
+  const int64_t tiles = (a.f + 127) / 128;
+  if (gx > 0x7fffffffLL) return fail(GNN_ERR_UNSUPPORTED, "spmm: too many rows for one launch");
+  spmm_scalar_kernel<WM, MEAN, HOT, IdxT>
+      <<<dim3(static_cast<unsigned>(gx), static_cast<unsigned>(tiles)), threads, 0, stream>>>(a);
+  GNN_LAUNCH_CHECK("spmm scalar kernel launch");
+  return GNN_OK;
+}
+
+struct SpmmRequest {
+  const void* row_ptr;
+  int row_ptr_type;
+  const int32_t* col;
+  const float* dis;
+  const float* ew;
+  const float* x;
+  const float* hot;
+  int64_t hot_cutoff;
+  const int64_t* sched;
+  float* out;
+  int64_t n, nnz, f;
+  int64_t row_begin;
+  void* ws;
+  size_t ws_bytes;
+};
+
+template <int WM, int MEAN, bool HOT, class IdxT>
+int run_typed(const SpmmRequest& q, cudaStream_t stream) {
+  SpmmArgs a{};
+  a.row_ptr = q.row_ptr;
+  a.col = q.col;
+  a.dis = q.dis;
+  a.dis_row = q.dis != nullptr ? q.dis + q.row_begin : nullptr;
+  a.ew = q.ew;
+  a.x = q.x;
+  a.hot = q.hot;
+  a.hot_cutoff = q.hot_cutoff;
+  a.sched = q.sched;
+  a.out = q.out;
+  a.n = q.n;
+  a.f = q.f;
+
+  const uintptr_t align = reinterpret_cast<uintptr_t>(q.x) | reinterpret_cast<uintptr_t>(q.out) |
+                          reinterpret_cast<uintptr_t>(q.hot);
+  const bool vec = (q.f % 4 == 0) && (align % 16 == 0);
+  if (!vec) return launch_scalar<WM, MEAN, HOT, IdxT>(a, stream);
+
+  const int64_t tiles = ((q.f >> 2) + kTileF4 - 1) / kTileF4;
+  if (tiles > kMaxTiles) {
+    return fail(GNN_ERR_UNSUPPORTED, "spmm: feat_dim above " + std::to_string(kMaxTiles * 512) +
+                                         " is not supported");
+  }
+  a.long_thr = resolve_long_threshold(q.n, q.nnz);
+  a.long_cap = std::min<int64_t>(long_capacity(q.n, q.nnz), q.nnz / (a.long_thr + 1) + 1);
+  if (q.nnz <= a.long_thr) a.long_cap = 0;  // no row can be long
+  if (a.long_cap > 0) {
+    if (q.ws == nullptr || q.ws_bytes < gnn_spmm_workspace_bytes(q.n, q.nnz)) {
+      return fail(GNN_ERR_WORKSPACE, "spmm: workspace missing or smaller than gnn_spmm_workspace_bytes()");
+    }
+    a.counters = static_cast<uint32_t*>(q.ws);
+    a.long_list = reinterpret_cast<uint32_t*>(static_cast<char*>(q.ws) + kWsHeader);
+    GNN_CUDA_TRY(cudaMemsetAsync(q.ws, 0, kWsHeader, stream), "spmm: workspace reset");
+    const int threads = 256;
+    const int64_t want = (q.n + threads - 1) / threads;
+    const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, 8LL * sm_count())));
+    plan_long_rows_kernel<IdxT><<<blocks, threads, 0, stream>>>(
+        static_cast<const IdxT*>(q.row_ptr), q.n, a.long_thr, a.counters, a.long_list, a.long_cap);
+    GNN_LAUNCH_CHECK("spmm plan kernel launch");
+  } else {
+    a.long_thr = INT64_MAX;
+  }
+  return launch_vec<WM, MEAN, HOT, IdxT>(a, stream);
+}
+
+template <int WM, int MEAN>
+int run(const SpmmRequest& q, cudaStream_t stream) {
+  if (q.n < 0 || q.nnz < 0 || q.f < 0) {
+    return fail(GNN_ERR_INVALID_ARGUMENT, "num_nodes, num_edges and feat_dim must be >= 0");
+  }
+  if (q.row_ptr_type != GNN_INDEX_INT32 && q.row_ptr_type != GNN_INDEX_INT64) {
+    return fail(GNN_ERR_INVALID_ARGUMENT, "row_ptr must be int32 or int64");
+  }
+  if (q.row_ptr_type == GNN_INDEX_INT32 && q.nnz > INT32_MAX) {
+    return fail(GNN_ERR_INVALID_ARGUMENT, "num_edges exceeds int32 row_ptr range; use int64 row_ptr");
+  }
+  if (q.n > INT32_MAX) return fail(GNN_ERR_INVALID_ARGUMENT, "num_nodes must fit int32 column ids");
+  if (q.n == 0 || q.f == 0) {
+    clear_error();
+    return GNN_OK;
+  }
+  GNN_REQUIRE(q.row_ptr != nullptr, GNN_ERR_NULL_POINTER, "row_ptr must not be NULL");
+  GNN_REQUIRE(q.x != nullptr && q.out != nullptr, GNN_ERR_NULL_POINTER, "x and out must not be NULL");
+  if (q.nnz > 0) {
+    GNN_REQUIRE(q.col != nullptr, GNN_ERR_NULL_POINTER, "col_ind must not be NULL");
+    if (WM == kGcn) GNN_REQUIRE(q.dis != nullptr, GNN_ERR_NULL_POINTER, "deg_inv_sqrt must not be NULL");
+    if (WM == kEdge) GNN_REQUIRE(q.ew != nullptr, GNN_ERR_NULL_POINTER, "edge_weight must not be NULL");
+  }
+  if (WM == kGcn) GNN_REQUIRE(q.dis != nullptr, GNN_ERR_NULL_POINTER, "deg_inv_sqrt must not be NULL");
+  int rc;
+  const bool hot = q.hot != nullptr;
+  if (q.row_ptr_type == GNN_INDEX_INT64) {
+    rc = hot ? run_typed<WM, MEAN, true, int64_t>(q, stream) : run_typed<WM, MEAN, false, int64_t>(q, stream);
+  } else {
+    rc = hot ? run_typed<WM, MEAN, true, int32_t>(q, stream) : run_typed<WM, MEAN, false, int32_t>(q, stream);
+  }
+  if (rc == GNN_OK) clear_error();
+  return rc;
+}
+
+int check_optimized(const int64_t* sched, const float* hot, int64_t cutoff, int64_t n) {
+  GNN_REQUIRE(sched != nullptr, GNN_ERR_NULL_POINTER, "row_schedule must be CUDA");
+  GNN_REQUIRE(hot != nullptr, GNN_ERR_NULL_POINTER, "hot_feature_cache must be CUDA");
+  GNN_REQUIRE(cutoff >= 1, GNN_ERR_INVALID_ARGUMENT, "hot_node_cutoff must be >= 1");
+  GNN_REQUIRE(cutoff <= n, GNN_ERR_INVALID_ARGUMENT, "hot_node_cutoff must be <= num_nodes");
+  return GNN_OK;
+}
+
+__global__ void stage_pages_kernel(const int64_t* __restrict__ page_ids, const float* __restrict__ x,
+                                   float* __restrict__ out, int64_t total_rows, int64_t rows_per_page,
+                                   int64_t f, int64_t n) {
+  const int64_t count = total_rows * f;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count; i += stride) {
+    const int64_t cached_row = i / f;
+    const int64_t feat = i - cached_row * f;
+    const int64_t page_slot = cached_row / rows_per_page;
+    const int64_t node = page_ids[page_slot] * rows_per_page + (cached_row - page_slot * rows_per_page);
+    out[i] = (node >= 0 && node < n) ? x[node * f + feat] : 0.0f;
+  }
+}
+
+__global__ void copy_rows_kernel(const float* __restrict__ x, float* __restrict__ out, int64_t count) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count; i += stride) {
+    out[i] = x[i];
+  }
+}
+
+}  // namespace
+}  // namespace gnnb200
+
+using namespace gnnb200;
+
+extern "C" size_t gnn_spmm_workspace_bytes(int64_t num_nodes, int64_t num_edges) {
+  if (num_nodes <= 0 || num_edges < 0) return kWsHeader;
+  const int64_t cap = long_capacity(num_nodes, num_edges);
+  const size_t list = (static_cast<size_t>(cap) * sizeof(uint32_t) + 255) & ~static_cast<size_t>(255);
+  return kWsHeader + list;
+}
+
+static SpmmRequest make_req(const void* rp, int rpt, const int32_t* col, const float* dis,
+                            const float* ew, const float* x, float* out, int64_t n, int64_t nnz,
+                            int64_t f, void* ws, size_t wsb) {
+  SpmmRequest q{};
+  q.row_ptr = rp;
+  q.row_ptr_type = rpt;
+  q.col = col;
+  q.dis = dis;
+  q.ew = ew;
+  q.x = x;
+  q.out = out;
+  q.n = n;
+  q.nnz = nnz;
+  q.f = f;
+  q.ws = ws;
+  q.ws_bytes = wsb;
+  return q;
+}
+
+extern "C" int gnn_spmm_gcn_forward(const void* row_ptr, int row_ptr_type, const int32_t* col_ind,
+                                    const float* deg_inv_sqrt, const float* x, float* out,
+                                    int64_t num_nodes, int64_t num_edges, int64_t feat_dim,
+                                    void* workspace, size_t workspace_bytes, gnn_stream_t stream) {
+  auto q = make_req(row_ptr, row_ptr_type, col_ind, deg_inv_sqrt, nullptr, x, out, num_nodes,
+                    num_edges, feat_dim, workspace, workspace_bytes);
+  return run<kGcn, kNoMean>(q, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int gnn_spmm_gcn_partition_forward(const void* row_ptr, int row_ptr_type,
+                                              const int32_t* col_ind, const float* deg_inv_sqrt,
+                                              int64_t row_begin, const float* x, float* out,
+                                              int64_t num_rows, int64_t num_cols, int64_t num_edges,
+                                              int64_t feat_dim, void* workspace, size_t workspace_bytes,
+                                              gnn_stream_t stream) {
+  GNN_REQUIRE(row_begin >= 0 && num_rows >= 0 && row_begin + num_rows <= num_cols, GNN_ERR_INVALID_ARGUMENT,
+              "shard rows [row_begin, row_begin + num_rows) must lie inside [0, num_cols)");
+  GNN_REQUIRE(num_cols <= INT32_MAX, GNN_ERR_INVALID_ARGUMENT, "num_cols must fit int32 column ids");
+  auto q = make_req(row_ptr, row_ptr_type, col_ind, deg_inv_sqrt, nullptr, x, out, num_rows,
+                    num_edges, feat_dim, workspace, workspace_bytes);
+  q.row_begin = row_begin;
+  return run<kGcn, kNoMean>(q, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int gnn_spmm_gcn_hmm_forward(const void* row_ptr, int row_ptr_type, const int32_t* col_ind,
+                                        const float* deg_inv_sqrt, const float* x, float* out,
+                                        int64_t num_nodes, int64_t num_edges, int64_t feat_dim,
+                                        void* workspace, size_t workspace_bytes, gnn_stream_t stream) {
+  return gnn_spmm_gcn_forward(row_ptr, row_ptr_type, col_ind, deg_inv_sqrt, x, out, num_nodes,
+                              num_edges, feat_dim, workspace, workspace_bytes, stream);
+}
+
+extern "C" int gnn_spmm_gcn_hmm_optimized_forward(
+    const void* row_ptr, int row_ptr_type, const int32_t* col_ind, const float* deg_inv_sqrt,
+    const float* x, const int64_t* row_schedule, const float* hot_feature_cache,
+    int64_t hot_node_cutoff, float* out, int64_t num_nodes, int64_t num_edges, int64_t feat_dim,
+    void* workspace, size_t workspace_bytes, gnn_stream_t stream) {
+  int rc = check_optimized(row_schedule, hot_feature_cache, hot_node_cutoff, num_nodes);
+  if (rc != GNN_OK) return rc;
+  auto q = make_req(row_ptr, row_ptr_type, col_ind, deg_inv_sqrt, nullptr, x, out, num_nodes,
+                    num_edges, feat_dim, workspace, workspace_bytes);
+  q.sched = row_schedule;
+  q.hot = hot_feature_cache;
+  q.hot_cutoff = hot_node_cutoff;
+  return run<kGcn, kNoMean>(q, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int gnn_spmm_pyg_gcn_forward(const void* row_ptr, int row_ptr_type, const int32_t* col_ind,
+                                        const float* edge_weight, const float* x, float* out,
+                                        int64_t num_nodes, int64_t num_edges, int64_t feat_dim,
+                                        void* workspace, size_t workspace_bytes, gnn_stream_t stream) {
+  auto q = make_req(row_ptr, row_ptr_type, col_ind, nullptr, edge_weight, x, out, num_nodes,
+                    num_edges, feat_dim, workspace, workspace_bytes);
+  return run<kEdge, kNoMean>(q, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int gnn_spmm_pyg_gcn_plain_forward(const void* row_ptr, int row_ptr_type,
+                                              const int32_t* col_ind, const float* edge_weight,
+                                              const float* x, float* out, int64_t num_nodes,
+                                              int64_t num_edges, int64_t feat_dim, void* workspace,
+                                              size_t workspace_bytes, gnn_stream_t stream) {
+  return gnn_spmm_pyg_gcn_forward(row_ptr, row_ptr_type, col_ind, edge_weight, x, out, num_nodes,
+                                  num_edges, feat_dim, workspace, workspace_bytes, stream);
+}
+
+extern "C" int gnn_spmm_pyg_gcn_optimized_forward(
+    const void* row_ptr, int row_ptr_type, const int32_t* col_ind, const float* edge_weight,
+    const float* x, const int64_t* row_schedule, const float* hot_feature_cache,
+    int64_t hot_node_cutoff, float* out, int64_t num_nodes, int64_t num_edges, int64_t feat_dim,
+    void* workspace, size_t workspace_bytes, gnn_stream_t stream) {
+  int rc = check_optimized(row_schedule, hot_feature_cache, hot_node_cutoff, num_nodes);
+  if (rc != GNN_OK) return rc;
+  auto q = make_req(row_ptr, row_ptr_type, col_ind, nullptr, edge_weight, x, out, num_nodes,
+                    num_edges, feat_dim, workspace, workspace_bytes);
+  q.sched = row_schedule;
+  q.hot = hot_feature_cache;
+  q.hot_cutoff = hot_node_cutoff;
+  return run<kEdge, kNoMean>(q, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int gnn_spmm_sum_forward(const void* row_ptr, int row_ptr_type, const int32_t* col_ind,
+                                    const float* x, float* out, int64_t num_nodes, int64_t num_edges,
+                                    int64_t feat_dim, void* workspace, size_t workspace_bytes,
+                                    gnn_stream_t stream) {
+  auto q = make_req(row_ptr, row_ptr_type, col_ind, nullptr, nullptr, x, out, num_nodes, num_edges,
+                    feat_dim, workspace, workspace_bytes);
+  return run<kUnit, kNoMean>(q, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int gnn_spmm_mean_forward(const void* row_ptr, int row_ptr_type, const int32_t* col_ind,
+                                     const float* x, float* out, int64_t num_nodes, int64_t num_edges,
+                                     int64_t feat_dim, int reciprocal, void* workspace,
+                                     size_t workspace_bytes, gnn_stream_t stream) {
+  auto q = make_req(row_ptr, row_ptr_type, col_ind, nullptr, nullptr, x, out, num_nodes, num_edges,
+                    feat_dim, workspace, workspace_bytes);
+  if (reciprocal) return run<kUnit, kMeanRcp>(q, reinterpret_cast<cudaStream_t>(stream));
+  return run<kUnit, kMeanDiv>(q, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int gnn_stage_feature_pages(const int64_t* page_ids, int64_t num_pages, const float* x,
+                                       int64_t num_nodes, float* out, int64_t rows_per_page,
+                                       int64_t feat_dim, gnn_stream_t stream) {
+  GNN_REQUIRE(rows_per_page >= 1, GNN_ERR_INVALID_ARGUMENT, "rows_per_page must be >= 1");
+  GNN_REQUIRE(num_pages >= 0 && feat_dim >= 0 && num_nodes >= 0, GNN_ERR_INVALID_ARGUMENT,
+              "sizes must be >= 0");
+  const int64_t total_rows = num_pages * rows_per_page;
+  const int64_t count = total_rows * feat_dim;
+  if (count == 0) {
+    clear_error();
+    return GNN_OK;
+  }
+  GNN_REQUIRE(page_ids && x && out, GNN_ERR_NULL_POINTER, "page_ids, x and out must not be NULL");
+  const int threads = 256;
+  const int blocks = static_cast<int>(std::min<int64_t>((count + threads - 1) / threads, 16LL * sm_count()));
+  stage_pages_kernel<<<blocks, threads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      page_ids, x, out, total_rows, rows_per_page, feat_dim, num_nodes);
+  GNN_LAUNCH_CHECK("stage_feature_pages launch");
+  clear_error();
+  return GNN_OK;
+}
+
+extern "C" int gnn_stage_feature_rows(const float* x, int64_t x_rows, float* out, int64_t out_rows,
+                                      int64_t feat_dim, gnn_stream_t stream) {
+  GNN_REQUIRE(out_rows <= x_rows, GNN_ERR_INVALID_ARGUMENT,
+              "out rows must be <= x rows for staged prefix copies");
+  GNN_REQUIRE(out_rows >= 0 && feat_dim >= 0, GNN_ERR_INVALID_ARGUMENT, "sizes must be >= 0");
+  const int64_t count = out_rows * feat_dim;
+  if (count == 0) {
+    clear_error();
+    return GNN_OK;
+  }
+  GNN_REQUIRE(x && out, GNN_ERR_NULL_POINTER, "x and out must not be NULL");
+  const int threads = 256;
+  const int blocks = static_cast<int>(std::min<int64_t>((count + threads - 1) / threads, 16LL * sm_count()));
+  copy_rows_kernel<<<blocks, threads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(x, out, count);
+  GNN_LAUNCH_CHECK("stage_feature_rows launch");
+  clear_error();
+  return GNN_OK;
+}

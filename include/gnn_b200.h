@@ -1,0 +1,256 @@
+/*
+ * gnn_b200.h — C ABI of libgnnb200.so, the B200 (sm_100a) GNN aggregation engine.
+ *
+ * Drop-in boundary for the operator surface of jonghyun1215/GNN_cuda. Every
+ * entry point replaces one function of the reference's pybind11 tables
+ * (GNN_cuda_common/native/{agg_ops,gcn_ops,pyg_gcn_ops,uvm_allocator}.cpp);
+ * the comment above each declaration names the reference function (file:line)
+ * that it replaces.
+ *
+ * Conventions
+ *   - Plain pointers and sizes only. Device pointers must be readable by the
+ *     current CUDA device (device memory, cudaMallocManaged memory, mapped
+ *     pinned host memory, or pageable host memory on HMM-capable systems).
+ *   - Dense matrices are row-major, contiguous, fp32. Index arrays: row_ptr is
+ *     int32 or int64 (see gnn_index_type), col_ind is int32.
+ *   - Every call is asynchronous on `stream` (a cudaStream_t; NULL = legacy
+ *     default stream) and returns a gnn_status. On failure, gnn_last_error()
+ *     returns a thread-local message whose text matches the reference's
+ *     TORCH_CHECK messages where the same condition is checked.
+ *   - No entry point allocates device memory except the allocator family
+ *     (gnn_managed_*). Kernels that need scratch take a caller-provided
+ *     workspace whose size is given by the matching *_workspace_bytes query.
+ *   - Results are deterministic: no floating-point atomics; every output row
+ *     is reduced in a fixed order.
+ */
+#ifndef GNN_B200_H_
+#define GNN_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* The library is built with hidden visibility; everything declared here is exported. */
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+typedef struct CUstream_st* gnn_stream_t; /* == cudaStream_t */
+
+typedef enum gnn_status {
+  GNN_OK = 0,
+  GNN_ERR_INVALID_ARGUMENT = 1, /* shape / size / range check failed          */
+  GNN_ERR_NULL_POINTER = 2,     /* a required pointer was NULL                */
+  GNN_ERR_UNSUPPORTED = 3,      /* valid request this build does not support  */
+  GNN_ERR_CUDA = 4,             /* a CUDA runtime call or launch failed       */
+  GNN_ERR_TIMEOUT = 5,          /* a bounded device-side wait gave up         */
+  GNN_ERR_DEVICE = 6,           /* no usable CUDA device / capability missing */
+  GNN_ERR_WORKSPACE = 7         /* workspace missing or too small             */
+} gnn_status;
+
+typedef enum gnn_index_type {
+  GNN_INDEX_INT32 = 0,
+  GNN_INDEX_INT64 = 1
+} gnn_index_type;
+
+/* Precision of the dense transform X·W on the tensor cores. */
+typedef enum gnn_precision {
+  GNN_PRECISION_TF32 = 0, /* one tf32 tcgen05 pass (north-star tolerance 2e-3)   */
+  GNN_PRECISION_FP32 = 1  /* fp32 SIMT FFMA, the reference's cublasSgemm numerics */
+} gnn_precision;
+
+/* ---- library --------------------------------------------------------------- */
+int gnn_version(void);                /* major*10000 + minor*100 + patch */
+const char* gnn_last_error(void);     /* thread-local; "" after a success  */
+const char* gnn_status_string(int status);
+/* Tuning knobs (process-wide). Names: "spmm.long_row_threshold" (edges; 0 =
+ * automatic), "spmm.long_row_warps" (4..16). Returns GNN_ERR_INVALID_ARGUMENT
+ * for an unknown name or out-of-range value. */
+int gnn_config_set_int(const char* name, int64_t value);
+int gnn_config_get_int(const char* name, int64_t* value);
+/* Number of kernels this library has launched in this process (all devices). */
+uint64_t gnn_kernel_launches(void);
+/* 1 when GNN_PRECISION_TF32 GEMMs of this shape run on the tcgen05 tensor
+ * cores of the current device, 0 when they run on the FFMA kernel. */
+int gnn_gemm_uses_tensor_cores(int64_t m, int64_t k, int64_t n);
+
+/* ---- CSR aggregation (SpMM) ------------------------------------------------
+ * All aggregation entry points compute, for every row r of a dst-major CSR,
+ *     out[r, :] = epilogue( sum_{e in row r, CSR order} w_e * x[col_ind[e], :] )
+ * into a preallocated `out` of the same shape as `x` ([num_nodes, feat_dim]).
+ * Rows of degree <= the long-row threshold are accumulated sequentially in CSR
+ * order with fused multiply-adds, exactly like the reference kernels; longer
+ * rows are split across the warps of one CTA and the partial sums are added in
+ * a fixed order.
+ *
+ * `workspace` must hold gnn_spmm_workspace_bytes(num_nodes, num_edges) bytes
+ * (256-byte aligned, device memory). Two calls in flight at once on different
+ * streams must use different workspaces.
+ */
+size_t gnn_spmm_workspace_bytes(int64_t num_nodes, int64_t num_edges);
+
+/* GCN normalised aggregation, w_e = deg_inv_sqrt[r] * deg_inv_sqrt[col].
+ * Replaces spmm_gcn_forward_cuda_ (naive), GNN_cuda_common/native/gcn_ops.cu:327. */
+int gnn_spmm_gcn_forward(const void* row_ptr, int row_ptr_type, const int32_t* col_ind,
+                         const float* deg_inv_sqrt, const float* x, float* out,
+                         int64_t num_nodes, int64_t num_edges, int64_t feat_dim,
+                         void* workspace, size_t workspace_bytes, gnn_stream_t stream);
+
+/* Row-partitioned GCN aggregation for one shard of a multi-GPU run (no
+ * reference counterpart; the reference is single-GPU). The shard holds rows
+ * [row_begin, row_begin + num_rows) of the global CSR: row_ptr/col_ind are the
+ * shard's (col_ind keeps global column ids), deg_inv_sqrt and x are global
+ * ([num_cols] and [num_cols, feat_dim]), out is [num_rows, feat_dim]. Same
+ * arithmetic as gnn_spmm_gcn_forward with dis[row_begin + r] as row scale. */
+int gnn_spmm_gcn_partition_forward(const void* row_ptr, int row_ptr_type, const int32_t* col_ind,
+                                   const float* deg_inv_sqrt, int64_t row_begin, const float* x,
+                                   float* out, int64_t num_rows, int64_t num_cols, int64_t num_edges,
+                                   int64_t feat_dim, void* workspace, size_t workspace_bytes,
+                                   gnn_stream_t stream);
+
+/* Replaces spmm_gcn_hmm_forward_cuda_ ("plain", the default GCN kernel),
+ * GNN_cuda_common/native/gcn_ops.cu:350. Same arithmetic as the naive entry. */
+int gnn_spmm_gcn_hmm_forward(const void* row_ptr, int row_ptr_type, const int32_t* col_ind,
+                             const float* deg_inv_sqrt, const float* x, float* out,
+                             int64_t num_nodes, int64_t num_edges, int64_t feat_dim,
+                             void* workspace, size_t workspace_bytes, gnn_stream_t stream);
+
+/* Row-scheduled variant with a device copy of the first `hot_node_cutoff` rows
+ * of x: neighbours col < hot_node_cutoff are read from hot_feature_cache.
+ * Replaces spmm_gcn_hmm_optimized_forward_cuda_, gcn_ops.cu:381 (checks :260-285). */
+int gnn_spmm_gcn_hmm_optimized_forward(const void* row_ptr, int row_ptr_type,
+                                       const int32_t* col_ind, const float* deg_inv_sqrt,
+                                       const float* x, const int64_t* row_schedule,
+                                       const float* hot_feature_cache, int64_t hot_node_cutoff,
+                                       float* out, int64_t num_nodes, int64_t num_edges,
+                                       int64_t feat_dim, void* workspace, size_t workspace_bytes,
+                                       gnn_stream_t stream);
+
+/* out[i, :] = x[page_ids[i / rows_per_page] * rows_per_page + i % rows_per_page, :] or 0
+ * past num_nodes. Replaces stage_feature_pages_cuda_, gcn_ops.cu:426. */
+int gnn_stage_feature_pages(const int64_t* page_ids, int64_t num_pages, const float* x,
+                            int64_t num_nodes, float* out, int64_t rows_per_page,
+                            int64_t feat_dim, gnn_stream_t stream);
+
+/* out[:rows] = x[:rows]. Replaces stage_feature_rows_cuda_, gcn_ops.cu:449. */
+int gnn_stage_feature_rows(const float* x, int64_t x_rows, float* out, int64_t out_rows,
+                           int64_t feat_dim, gnn_stream_t stream);
+
+/* PyG-style weighted aggregation, w_e = edge_weight[e].
+ * Replaces spmm_pyg_gcn_forward_cuda_ (naive), pyg_gcn_ops.cu:254. */
+int gnn_spmm_pyg_gcn_forward(const void* row_ptr, int row_ptr_type, const int32_t* col_ind,
+                             const float* edge_weight, const float* x, float* out,
+                             int64_t num_nodes, int64_t num_edges, int64_t feat_dim,
+                             void* workspace, size_t workspace_bytes, gnn_stream_t stream);
+
+/* Replaces spmm_pyg_gcn_plain_forward_cuda_, pyg_gcn_ops.cu:277. */
+int gnn_spmm_pyg_gcn_plain_forward(const void* row_ptr, int row_ptr_type,
+                                   const int32_t* col_ind, const float* edge_weight,
+                                   const float* x, float* out, int64_t num_nodes,
+                                   int64_t num_edges, int64_t feat_dim, void* workspace,
+                                   size_t workspace_bytes, gnn_stream_t stream);
+
+/* Replaces spmm_pyg_gcn_hmm_optimized_forward_cuda_ (pyg_gcn_ops.cu:353) and
+ * spmm_pyg_gcn_uvm_optimized_forward_cuda_ (pyg_gcn_ops.cu:363), which are the
+ * same function in the reference. */
+int gnn_spmm_pyg_gcn_optimized_forward(const void* row_ptr, int row_ptr_type,
+                                       const int32_t* col_ind, const float* edge_weight,
+                                       const float* x, const int64_t* row_schedule,
+                                       const float* hot_feature_cache, int64_t hot_node_cutoff,
+                                       float* out, int64_t num_nodes, int64_t num_edges,
+                                       int64_t feat_dim, void* workspace, size_t workspace_bytes,
+                                       gnn_stream_t stream);
+
+/* Sum aggregation (GIN). Replaces spmm_sum_forward_cuda_, agg_ops.cu:315, and
+ * spmm_sum_hmm_forward_cuda_, agg_ops.cu:329 (identical arithmetic). */
+int gnn_spmm_sum_forward(const void* row_ptr, int row_ptr_type, const int32_t* col_ind,
+                         const float* x, float* out, int64_t num_nodes, int64_t num_edges,
+                         int64_t feat_dim, void* workspace, size_t workspace_bytes,
+                         gnn_stream_t stream);
+
+/* Mean aggregation (GraphSAGE); a row of degree 0 gives 0.
+ * reciprocal == 0: acc / deg, as spmm_mean_forward_cuda_, agg_ops.cu:322 (kernel :40-45).
+ * reciprocal != 0: acc * (1/deg), as spmm_mean_hmm_forward_cuda_, agg_ops.cu:336 (kernel :102-111). */
+int gnn_spmm_mean_forward(const void* row_ptr, int row_ptr_type, const int32_t* col_ind,
+                          const float* x, float* out, int64_t num_nodes, int64_t num_edges,
+                          int64_t feat_dim, int reciprocal, void* workspace,
+                          size_t workspace_bytes, gnn_stream_t stream);
+
+/* ---- dense transform and epilogues ----------------------------------------- */
+
+/* out[M,N] = x[M,K] · weight[K,N] (weight stored [in, out] = nn.Linear.weight^T).
+ * Replaces gemm_forward_cuda_, agg_ops.cu:369 (cublasSgemm). */
+int gnn_gemm_forward(const float* x, const float* weight, float* out, int64_t m, int64_t k,
+                     int64_t n, int precision, gnn_stream_t stream);
+
+/* out = relu?(x · weight + bias) with bias/ReLU fused into the GEMM epilogue;
+ * bias may be NULL. Replaces linear_forward_cuda_, agg_ops.cu:343. */
+int gnn_linear_forward(const float* x, const float* weight, const float* bias, float* out,
+                       int64_t m, int64_t k, int64_t n, int relu, int precision,
+                       gnn_stream_t stream);
+
+/* out[i, j] = relu?(out[i, j] + bias[j]); bias may be NULL.
+ * Replaces bias_relu_forward_cuda_, agg_ops.cu:393 (kernel :132-147). */
+int gnn_bias_relu_forward(float* out, const float* bias, int64_t rows, int64_t cols, int relu,
+                          gnn_stream_t stream);
+
+/* dst += alpha * src (one fused multiply-add per element).
+ * Replaces tensor_add_inplace_cuda_, agg_ops.cu:399 (kernel :149-156). */
+int gnn_tensor_add_inplace(float* dst, const float* src, float alpha, int64_t count,
+                           gnn_stream_t stream);
+
+/* t = max(t, 0) keeping -0 and NaN as they are. Replaces relu_inplace_cuda_, agg_ops.cu:420. */
+int gnn_relu_inplace(float* t, int64_t count, gnn_stream_t stream);
+
+/* ---- unified / host memory (allocator family) ------------------------------ */
+
+/* cudaMallocManaged(bytes, cudaMemAttachGlobal) on `device`; *ptr = NULL for 0 bytes.
+ * Replaces managed_empty_cuda, uvm_allocator.cu:93. */
+int gnn_managed_alloc(size_t bytes, int device, void** ptr);
+/* Frees memory from gnn_managed_alloc (deleter of uvm_allocator.cu:107-113). */
+int gnn_managed_free(void* ptr, int device);
+/* *supported = cudaDevAttrPageableMemoryAccess of `device` (HMM). Replaces the
+ * capability check of hmm_empty_cpu, uvm_allocator.cu:45-57 and :120-127. */
+int gnn_hmm_supported(int device, int* supported);
+/* Host memcpy into managed memory after checking that dst is managed.
+ * Replaces copy_cpu_to_managed_cuda_, uvm_allocator.cu:129. */
+int gnn_copy_host_to_managed(void* dst, const void* src, size_t bytes);
+/* cudaMemPrefetchAsync of [ptr+offset, ptr+offset+bytes) to `location`
+ * (-1 = cpu, >=0 = that device) on `stream`. Replaces prefetch_cuda_ (:151)
+ * and prefetch_range_cuda_ (:163) of uvm_allocator.cu; the reference always
+ * used the default stream, this entry point takes the caller's stream. */
+int gnn_prefetch(void* ptr, size_t offset, size_t bytes, size_t total_bytes, int location,
+                 int device, gnn_stream_t stream);
+/* cudaMemAdvise wrappers. location -1 = cpu, 0 = `device` (the reference's
+ * location_code convention, uvm_allocator.cu:189-229). */
+int gnn_advise_preferred_location(void* ptr, size_t bytes, int location, int device);
+int gnn_advise_accessed_by(void* ptr, size_t bytes, int location, int device);
+int gnn_advise_read_mostly(void* ptr, size_t bytes, int enabled, int device);
+
+typedef struct gnn_pointer_info {
+  int memory_type;     /* 0 unregistered, 1 host, 2 device, 3 managed, -1 query failed */
+  int device;          /* attribute device, -1 if none                                   */
+  int is_managed;
+  int is_host_mapped;  /* pinned host memory with a device alias                         */
+  int pageable_access; /* current device supports HMM pageable access                    */
+  void* device_pointer;
+} gnn_pointer_info;
+/* Replaces pointer_info_cuda, uvm_allocator.cu:231 (the Python layer builds the dict). */
+int gnn_pointer_info_query(const void* ptr, gnn_pointer_info* info);
+/* Device-usable alias of a host pointer: the mapped alias of pinned memory, the
+ * pointer itself under HMM, else GNN_ERR_DEVICE. Replaces
+ * get_device_accessible_void_ptr, tensor_access.cuh:25-64. */
+int gnn_device_accessible_ptr(const void* host_ptr, void** device_ptr);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* GNN_B200_H_ */

@@ -1,0 +1,105 @@
+"""The C-ABI library on a machine without a GPU: it loads, exports every symbol
+that include/gnn_b200.h declares, and rejects bad arguments with the right
+status codes before touching the device. Also the Python-layer checks that
+mirror the reference's TORCH_CHECK messages."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+from gnn_cuda_b200 import _native as N
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _header_functions() -> list[str]:
+    text = (ROOT / "include" / "gnn_b200.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(gnn_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(str(N.LIB_PATH))
+    names = _header_functions()
+    assert len(names) >= 30
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_python_prototypes_cover_header():
+    assert set(_header_functions()) == set(N.PROTOTYPES)
+
+
+def test_version_and_status_strings():
+    assert N.lib().gnn_version() >= 100
+    assert N.lib().gnn_status_string(0) == b"ok"
+    assert N.lib().gnn_status_string(7) == b"workspace error"
+
+
+def test_invalid_arguments_rejected_without_device():
+    L = N.lib()
+    rc = L.gnn_spmm_sum_forward(None, 0, None, None, None, -1, 0, 4, None, 0, None)
+    assert rc == 1 and "must be >= 0" in N.last_error()
+    rc = L.gnn_spmm_sum_forward(None, 5, None, None, None, 3, 0, 4, None, 0, None)
+    assert rc == 1 and "int32 or int64" in N.last_error()
+    rc = L.gnn_spmm_sum_forward(None, 0, None, None, None, 3, 0, 4, None, 0, None)
+    assert rc == 2 and "row_ptr" in N.last_error()
+    rc = L.gnn_spmm_sum_forward(None, 0, None, None, None, 3, 1 << 33, 4, None, 0, None)
+    assert rc == 1 and "int64 row_ptr" in N.last_error()
+    # empty problems are valid no-ops
+    assert L.gnn_spmm_sum_forward(None, 0, None, None, None, 0, 0, 4, None, 0, None) == 0
+    assert L.gnn_gemm_forward(None, None, None, 0, 5, 5, 0, None) == 0
+    assert L.gnn_gemm_forward(None, None, None, 4, 5, 5, 9, None) == 1
+    rc = L.gnn_spmm_gcn_hmm_optimized_forward(None, 0, None, None, None, None, None, 0, None, 4, 0, 4, None, 0, None)
+    assert rc == 2 and "row_schedule must be CUDA" in N.last_error()
+    assert L.gnn_stage_feature_rows(None, 3, None, 4, 2, None) == 1
+    assert "out rows must be <= x rows" in N.last_error()
+    assert L.gnn_prefetch(None, 8, 4, 10, 0, 0, None) == 1
+    assert "exceeds tensor byte size" in N.last_error()
+
+
+def test_workspace_size_query():
+    L = N.lib()
+    assert L.gnn_spmm_workspace_bytes(0, 0) == 256
+    small = L.gnn_spmm_workspace_bytes(1000, 5000)
+    big = L.gnn_spmm_workspace_bytes(2_449_029, 64_308_169)
+    assert 256 < small < big < 16 * 2**20
+
+
+def test_config_knobs():
+    old = N.config_get("spmm.long_row_threshold")
+    N.config_set("spmm.long_row_threshold", 64)
+    assert N.config_get("spmm.long_row_threshold") == 64
+    N.config_set("spmm.long_row_threshold", old)
+    with pytest.raises(RuntimeError, match="unknown config key"):
+        N.config_set("nope", 1)
+    with pytest.raises(RuntimeError, match=r"\[4, 16\]"):
+        N.config_set("spmm.long_row_warps", 64)
+
+
+def test_python_checks_match_reference_messages():
+    from gnn_cuda_b200.GNN_cuda_common import agg_ops, gcn_ops
+    rp = torch.zeros(3, dtype=torch.int32)
+    ci = torch.zeros(0, dtype=torch.int32)
+    x = torch.zeros(2, 4)
+    with pytest.raises(RuntimeError, match="out must be CUDA"):
+        agg_ops.spmm_sum_forward_(rp, ci, x, torch.zeros(2, 4))
+    with pytest.raises(RuntimeError, match="out must be CUDA"):
+        gcn_ops.spmm_gcn_forward_(rp, ci, torch.ones(2), x, torch.zeros(2, 4))
+    with pytest.raises(RuntimeError, match="out must be CUDA"):
+        agg_ops.gemm_forward_(x, torch.zeros(4, 3), torch.zeros(2, 3))
+
+
+def test_allocator_modes():
+    from gnn_cuda_b200.GNN_cuda_common import allocator as A
+    assert A.normalize_memory_mode("managed", allow_hmm=False) == "uvm"
+    assert A.normalize_memory_mode("torch_cuda", allow_hmm=True) == "device"
+    with pytest.raises(ValueError, match="'hmm' is graph-only"):
+        A.normalize_memory_mode("hmm", allow_hmm=False)
+    with pytest.raises(ValueError, match="Unsupported memory_mode"):
+        A.normalize_memory_mode("bogus", allow_hmm=True)
+    assert A.prefers_hmm_spmm("device", "hmm") and not A.prefers_hmm_spmm("uvm", "device")
+    with pytest.raises(ValueError, match="requires a CUDA device"):
+        A.managed_empty((2, 2), dtype=torch.float32, device=torch.device("cpu"))

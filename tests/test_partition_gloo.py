@@ -1,0 +1,90 @@
+"""Row partitioning and the between-layer row exchange, as world-size-2 gloo ranks on CPU.
+
+The CUDA aggregation is replaced here by the oracle (CPU test only): the test
+covers the host logic of the multi-GPU mode — equal-nnz bounds, shard
+construction with global column ids, and the broadcast-based exchange — and
+checks that the concatenated shard outputs equal the single-rank result bit for bit.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from gnn_cuda_b200 import partition, synth
+
+
+def test_bounds_balance_nnz():
+    u, v = synth.rmat_undirected(5000, 40000, seed=2)
+    s, d = synth.symmetrize(u, v)
+    from gnn_cuda_b200.GNN_cuda_common import graph_utils as G
+    g = G.build_gcn_normalized_csr(s, d, num_nodes=5000)
+    rp = g.row_ptr.numpy().astype(np.int64)
+    for world in (1, 2, 3, 4, 8):
+        b = partition.nnz_balanced_bounds(rp, world)
+        assert b[0] == 0 and b[-1] == 5000 and all(b[i] <= b[i + 1] for i in range(world))
+        loads = [rp[b[i + 1]] - rp[b[i]] for i in range(world)]
+        assert max(loads) - min(loads) <= rp[1:].max() - rp[:-1].min() + np.diff(rp).max() * 2
+    # one giant row heavier than a share keeps bounds monotone
+    rp2 = np.array([0, 1000, 1001, 1002, 1003], dtype=np.int64)
+    b = partition.nnz_balanced_bounds(rp2, 4)
+    assert b[0] == 0 and b[-1] == 4 and b == sorted(b)
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from oracle import oracle as O
+        from gnn_cuda_b200.GNN_cuda_common import graph_utils as G
+        n, f = 1200, 16
+        u, v = synth.rmat_undirected(n, 9000, seed=5)
+        s, d = synth.symmetrize(u, v)
+        g = G.build_gcn_normalized_csr(s, d, num_nodes=n)
+        x = synth.features(n, f, seed=6)
+        bounds = partition.nnz_balanced_bounds(g.row_ptr.numpy(), world)
+        shard = partition.make_shard(g.row_ptr, g.col_ind, bounds[rank], bounds[rank + 1])
+        # layer 1 on this shard's rows (oracle aggregation with global column ids)
+        rp_local = shard.row_ptr.numpy()
+        dis = g.deg_inv_sqrt.numpy()
+        # weight rows by dis[global row] * dis[col] through the edge-weight path
+        rows = np.repeat(np.arange(shard.num_rows) + shard.row_begin, np.diff(rp_local))
+        ew = (dis[rows] * dis[shard.col_ind.numpy()]).astype(np.float32)
+        out = O.spmm(rp_local, shard.col_ind.numpy(), x.numpy(), mode=O.W_EDGE, ew=ew)
+        full = torch.empty(n, f)
+        partition.exchange_rows(torch.from_numpy(out), full, bounds, rank)
+        q.put((rank, full.numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_exchange_matches_single_rank():
+    from oracle import oracle as O
+    from gnn_cuda_b200.GNN_cuda_common import graph_utils as G
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=120) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    n, f = 1200, 16
+    u, v = synth.rmat_undirected(n, 9000, seed=5)
+    s, d = synth.symmetrize(u, v)
+    g = G.build_gcn_normalized_csr(s, d, num_nodes=n)
+    x = synth.features(n, f, seed=6)
+    ref = O.spmm(g.row_ptr.numpy(), g.col_ind.numpy(), x.numpy(), mode=O.W_GCN, dis=g.deg_inv_sqrt.numpy())
+    for r in range(2):
+        assert np.array_equal(results[r].view(np.uint32), ref.view(np.uint32))
