@@ -57,7 +57,7 @@ def log(*a):
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--steps", type=int, default=60)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--seed", type=int, default=1)
@@ -324,11 +324,17 @@ def _cpu_rows_layer(O, hp, r0: int, r1: int, threads: int):
 
 
 def _cpu_sample_rows(O, hp, seconds: float, threads: int) -> tuple[int, float]:
+    """Rows [0, rows) whose one-layer oracle pass takes about `seconds`: grow a
+    probe until it runs for at least 1/8 of the target, then extrapolate."""
     n = hp["n"]
     probe = max(1, n // 512)
-    t0 = time.perf_counter()
-    _cpu_rows_layer(O, hp, 0, probe, threads)
-    dt = max(time.perf_counter() - t0, 1e-4)
+    while True:
+        t0 = time.perf_counter()
+        _cpu_rows_layer(O, hp, 0, probe, threads)
+        dt = max(time.perf_counter() - t0, 1e-4)
+        if dt >= seconds / 8 or probe >= n:
+            break
+        probe = min(n, probe * 4)
     rows = int(min(n, max(probe, probe * seconds / dt)))
     return rows, dt
 
