@@ -50,6 +50,7 @@ PROTOTYPES: dict[str, tuple[object, list[object]]] = {
         _i32, [_vp, _i32, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _sz, _vp]),
     "gnn_spmm_gcn_forward": (_i32, [_vp, _i32, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _sz, _vp]),
     "gnn_spmm_gcn_hmm_forward": (_i32, [_vp, _i32, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _sz, _vp]),
+    "gnn_spmm_gcn_forward_noalloc": (_i32, [_vp, _i32, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "gnn_spmm_gcn_hmm_optimized_forward": (
         _i32, [_vp, _i32, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _vp, _sz, _vp]),
     "gnn_stage_feature_pages": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _vp]),

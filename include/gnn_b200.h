@@ -111,6 +111,25 @@ int gnn_spmm_gcn_partition_forward(const void* row_ptr, int row_ptr_type, const 
                                    int64_t feat_dim, void* workspace, size_t workspace_bytes,
                                    gnn_stream_t stream);
 
+/* GCN aggregation that allocates nothing and takes no workspace. No
+ * counterpart in the reference: it exists for callers that cannot hand the
+ * library a scratch buffer or let it call cudaMalloc — a plugin host or FFI
+ * binding that owns all device memory and passes only inputs and outputs, a
+ * process pinned to a fixed memory budget, or a latency-critical path that
+ * cannot afford cudaMalloc/cudaFree (which may wait for the whole device).
+ * Same kernels and results as gnn_spmm_gcn_forward; the scratch is a built-in
+ * 8 MiB (8388608-byte) device array per GPU, held until the process exits.
+ * Problems with gnn_spmm_workspace_bytes(num_nodes, num_edges) > 8 MiB are
+ * rejected with GNN_ERR_UNSUPPORTED (for example, any graph with at most
+ * 2,097,088 nodes fits). All calls on a device share that array: calls that
+ * overlap on the GPU race and must be serialised (e.g. one stream). Each call
+ * clears the counters it reads. The first call on a device looks the array's
+ * address up, so make it before any stream capture on that device. */
+int gnn_spmm_gcn_forward_noalloc(const void* row_ptr, int row_ptr_type, const int32_t* col_ind,
+                                 const float* deg_inv_sqrt, const float* x, float* out,
+                                 int64_t num_nodes, int64_t num_edges, int64_t feat_dim,
+                                 gnn_stream_t stream);
+
 /* Replaces spmm_gcn_hmm_forward_cuda_ ("plain", the default GCN kernel),
  * GNN_cuda_common/native/gcn_ops.cu:350. Same arithmetic as the naive entry. */
 int gnn_spmm_gcn_hmm_forward(const void* row_ptr, int row_ptr_type, const int32_t* col_ind,
