@@ -45,6 +45,7 @@ PROTOTYPES: dict[str, tuple[object, list[object]]] = {
     "gnn_config_get_int": (_i32, [ctypes.c_char_p, ctypes.POINTER(_i64)]),
     "gnn_kernel_launches": (ctypes.c_uint64, []),
     "gnn_gemm_uses_tensor_cores": (_i32, [_i64, _i64, _i64]),
+    "gnn_device_status": (_i32, [_i32, ctypes.POINTER(_i32)]),
     "gnn_spmm_workspace_bytes": (_sz, [_i64, _i64]),
     "gnn_spmm_gcn_partition_forward": (
         _i32, [_vp, _i32, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _sz, _vp]),

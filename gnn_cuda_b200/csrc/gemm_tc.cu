@@ -1,23 +1,499 @@
-// tcgen05 (5th-generation tensor core) TF32 GEMM for the dense transform X·W.
-// Placeholder hook: until the tensor-core kernel is in place every request is
-// reported as not handled, and gemm_common runs the FFMA kernel.
+// tcgen05 (5th-generation tensor core) TF32 GEMM for the dense transform
+//   out[M, N] = relu?(X[M, K] · W[K, N] + bias)
+// replacing the reference's cublasSgemm call (GNN_cuda_common/native/agg_ops.cu:369-391)
+// plus its separate bias/ReLU pass (agg_ops.cu:132-147).
+//
+// Shape of the problem: M = number of nodes (millions), K = N = 128..256. At these
+// widths the GEMM is bound by HBM (read X once, write out once; 32-64 flop/B),
+// so the design keeps every byte moving once:
+//   * persistent CTAs, one per SM; each CTA owns one 128-column slice of W for
+//     the whole launch (staged once into shared memory, transposed to the
+//     K-major 128-byte-swizzled layout the MMA reads) and walks 128-row tiles of X;
+//   * warp 0 streams X tiles in 32-column (128-byte) swizzled chunks with TMA
+//     into a 4-stage ring; warp 1 issues tcgen05.mma (kind::tf32, M=128, N=BN,
+//     K=8 per instruction) into one of two TMEM accumulators; warps 2-5 drain
+//     the other accumulator (tcgen05.ld), add bias, apply ReLU and store fp32
+//     rows — so loads, MMAs and the epilogue of consecutive tiles overlap;
+//   * every mbarrier wait is bounded by a clock deadline; on expiry the kernel
+//     records an error code in a device status word, stops issuing work, waits
+//     (bounded) for its in-flight copies and MMAs, frees its TMEM and returns.
+// Accuracy: inputs are consumed as TF32 (10-bit mantissa), products accumulate
+// in fp32 — within the 2e-3 relative bound of the north-star tolerance.
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+
+#include <algorithm>
+#include <mutex>
+#include <string>
 
 #include "common.cuh"
 
 namespace gnnb200 {
+namespace {
 
-int gemm_tc_tf32(const float* x, const float* w, const float* bias, float* out, int64_t m,
-                 int64_t k, int64_t n, bool relu, cudaStream_t stream, bool* handled) {
-  (void)x; (void)w; (void)bias; (void)out; (void)m; (void)k; (void)n; (void)relu; (void)stream;
+constexpr int BM = 128;             // rows per tile (TMEM lanes)
+constexpr int KCHUNK = 32;          // tf32 elements per 128-byte swizzle row
+constexpr int STAGES = 4;           // X chunk ring depth
+constexpr int A_STAGE_BYTES = BM * KCHUNK * 4;  // 16 KiB
+constexpr int kThreads = 192;       // warp0 TMA, warp1 MMA/TMEM, warps 2-5 epilogue
+constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 2 GHz
+
+// device status word: 0 ok, otherwise the role that gave up waiting
+__device__ int g_tc_status = 0;
+
+struct TcParams {
+  int64_t m, k, n;
+  int64_t m_tiles;
+  int n_tiles;
+  const float* bias;
+  float* out;
+  int relu;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Waits for the phase of parity `parity` to complete; false after the deadline.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  const long long t0 = clock64();
+  while (true) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if (clock64() - t0 > kWaitCycles) return false;
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+      ::"r"(smem_u32(dst)), "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor, 128-byte swizzle, sm_100 version field = 1.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1) << 46;  // descriptor version (sm_100)
+  d |= static_cast<uint64_t>(2) << 61;  // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor: D f32, A/B tf32, both operands K-major, M x N.
+// (An MN-major B operand produced no output for kind::tf32 on B200 in our
+// tests, so W is staged transposed, K-major, instead.)
+__host__ __device__ constexpr uint32_t idesc_tf32(int m, int n) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | (0u << 15) | (0u << 16) |
+         (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+// Byte offset of element (row, k) in a K-major, 128-byte-swizzled operand made of
+// 32-column blocks: block kb = k / 32 holds `rows` rows of 128 B; inside each
+// 1024-byte group of 8 rows, 16-byte chunk c of row r sits at chunk c ^ (r % 8).
+__device__ __forceinline__ uint32_t kmajor_sw128_offset(int row, int k, int rows) {
+  const int kb = k >> 5;
+  const int chunk = (k & 31) >> 2;
+  return static_cast<uint32_t>(kb * rows * 128 + row * 128 + ((chunk ^ (row & 7)) << 4) + ((k & 3) << 2));
+}
+
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// Loads 32 consecutive fp32 columns of this thread's TMEM lane. The load and its
+// wait are one asm statement so no use of the registers can be scheduled
+// between the asynchronous load and its completion.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+
+__device__ __forceinline__ void record_timeout(int code) { atomicCAS(&g_tc_status, 0, code); }
+
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tf32_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const float* __restrict__ w, TcParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int K = static_cast<int>(p.k);
+  const int kchunks = K / KCHUNK;
+  const uint32_t w_bytes = static_cast<uint32_t>(BN) * K * 4;
+  uint8_t* sW = smem;                                  // K/32 blocks of [BN rows x 128 B], K-major
+  uint8_t* sA = smem + ((w_bytes + 1023) & ~1023u);    // STAGES x 16 KiB
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sA + STAGES * A_STAGE_BYTES);
+  uint64_t* full = bars;                 // [STAGES]
+  uint64_t* empty = bars + STAGES;       // [STAGES]
+  uint64_t* acc_full = bars + 2 * STAGES;      // [2]
+  uint64_t* acc_empty = bars + 2 * STAGES + 2; // [2]
+  uint64_t* drain = bars + 2 * STAGES + 5;     // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 6);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n_tile = blockIdx.x % p.n_tiles;
+  const int64_t m_first = blockIdx.x / p.n_tiles;
+  const int64_t m_step = gridDim.x / p.n_tiles;
+  constexpr uint32_t kTmemCols = 2 * BN;  // two accumulators; BN in {32, 64, 128}
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 4);
+    }
+    mbar_init(drain, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  // Stage this CTA's W slice (columns [n_tile*BN, +BN), all K rows) transposed
+  // into the K-major swizzled layout the MMA reads: row n of the operand is
+  // column n of W. Global reads are coalesced along n; the slice stays resident.
+  {
+    const float* wsrc = w + static_cast<int64_t>(n_tile) * BN;
+    for (int idx = threadIdx.x; idx < K * BN; idx += kThreads) {
+      const int k = idx / BN;
+      const int nn = idx - k * BN;
+      const float v = __ldg(wsrc + static_cast<int64_t>(k) * p.n + nn);
+      *reinterpret_cast<float*>(sW + kmajor_sw128_offset(nn, k, BN)) = v;
+    }
+    // generic-proxy smem writes -> visible to the tensor core (async proxy)
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap_x) : "memory");
+      int stage = 0;
+      uint32_t phase = 0;
+      int64_t issued = 0;
+      bool ok = true;
+      for (int64_t mt = m_first; mt < p.m_tiles && ok; mt += m_step) {
+        for (int kc = 0; kc < kchunks; ++kc) {
+          if (!mbar_wait(&empty[stage], phase ^ 1)) {
+            record_timeout(1);
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&full[stage], A_STAGE_BYTES);
+          tma_load_2d(sA + stage * A_STAGE_BYTES, &tmap_x, &full[stage], kc * KCHUNK, static_cast<int>(mt * BM));
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // drain: the last min(issued, STAGES) copies must have landed before exit
+      const int64_t pending = std::min<int64_t>(issued, STAGES);
+      for (int64_t i = 0; i < pending; ++i) {
+        if (--stage < 0) {
+          stage = STAGES - 1;
+          phase ^= 1;
+        }
+        if (!mbar_wait(&full[stage], phase)) record_timeout(5);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      constexpr uint32_t idesc = idesc_tf32(BM, BN);
+      const uint32_t sw_base = smem_u32(sW);
+      const uint32_t sa_base = smem_u32(sA);
+      bool ok = true;
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int64_t mt = m_first; mt < p.m_tiles && ok; mt += m_step) {
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1)) {
+          record_timeout(2);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kc = 0; kc < kchunks; ++kc) {
+          if (!mbar_wait(&full[stage], phase)) {
+            record_timeout(2);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < KCHUNK / 8; ++kk) {
+            // both operands K-major: 8 K values = 32 bytes along the 128-byte swizzled row
+            const uint64_t a_desc = sw128_desc(sa_base + stage * A_STAGE_BYTES + kk * 32, 16, 1024);
+            const uint64_t b_desc = sw128_desc(sw_base + kc * BN * 128 + kk * 32, 16, 1024);
+            mma_tf32(d_tmem, a_desc, b_desc, idesc, (kc | kk) != 0 ? 1u : 0u);
+          }
+          mma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit(&acc_full[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+      // all MMAs issued by this thread complete before TMEM is released
+      mma_commit(drain);
+      if (!mbar_wait(drain, 0)) record_timeout(6);
+    }
+  } else {
+    // ---------------- epilogue: warps 2..5 ----------------
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int row_in_tile = 32 * q + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    const int64_t ncol0 = static_cast<int64_t>(n_tile) * BN;
+    for (int64_t mt = m_first; mt < p.m_tiles; mt += m_step) {
+      // warp-uniform decision: the tcgen05.ld below is .sync.aligned
+      if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[acc], acc_phase))) {
+        if (lane == 0) record_timeout(3);
+        break;
+      }
+      tc_fence_after();
+      const int64_t row = mt * BM + row_in_tile;
+      float* orow = p.out + row * p.n + ncol0;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t r[32];
+        tmem_ld32(tmem_base + static_cast<uint32_t>(acc * BN + c0) + (static_cast<uint32_t>(32 * q) << 16), r);
+        if (row < p.m) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) {
+            float4 v = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
+                                   __uint_as_float(r[j + 3]));
+            if (p.bias != nullptr) v = add4(v, __ldg(reinterpret_cast<const float4*>(p.bias + ncol0 + c0 + j)));
+            if (p.relu) {
+              v.x = v.x < 0.0f ? 0.0f : v.x;
+              v.y = v.y < 0.0f ? 0.0f : v.y;
+              v.z = v.z < 0.0f ? 0.0f : v.z;
+              v.w = v.w < 0.0f ? 0.0f : v.w;
+            }
+            *reinterpret_cast<float4*>(orow + c0 + j) = v;
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols) : "memory");
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+    } else {
+      cudaGetLastError();
+    }
+  });
+  return fn;
+}
+
+bool device_is_sm100() {
+  int dev = 0, major = 0, minor = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  return major == 10 && minor == 0;
+}
+
+int pick_bn(int64_t n) {
+  if (n % 128 == 0) return 128;
+  if (n == 64) return 64;
+  if (n == 32) return 32;
+  return 0;
+}
+
+bool shape_ok(int64_t m, int64_t k, int64_t n) {
+  return m >= 1 && m <= (int64_t(1) << 31) - BM && k >= KCHUNK && k <= 256 && k % KCHUNK == 0 && pick_bn(n) != 0 &&
+         n <= 65536;
+}
+
+size_t smem_bytes(int bn, int64_t k) {
+  const size_t w = ((static_cast<size_t>(bn) * k * 4) + 1023) & ~size_t(1023);
+  return 1024 /* alignment slack */ + w + STAGES * A_STAGE_BYTES + 256 /* barriers + TMEM slot */;
+}
+
+template <int BN>
+int launch_bn(const float* x, const float* w, const float* bias, float* out, int64_t m, int64_t k, int64_t n,
+              bool relu, cudaStream_t stream) {
+  EncodeTiledFn enc = encode_fn();
+  if (enc == nullptr) return fail(GNN_ERR_DEVICE, "cuTensorMapEncodeTiled is not available from the driver");
+  CUtensorMap tx{};
+  {
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(m)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(k) * 4};
+    cuuint32_t box[2] = {KCHUNK, BM};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(x), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(GNN_ERR_CUDA, "cuTensorMapEncodeTiled(x) failed: " + std::to_string(r));
+  }
+  const size_t smem = smem_bytes(BN, k);
+  // the opt-in is a per-device function attribute; remember the largest size set per device
+  static int configured_smem[64][3] = {};
+  static std::mutex mu;
+  int dev = 0;
+  GNN_CUDA_TRY(cudaGetDevice(&dev), "cudaGetDevice");
+  const int slot = BN == 128 ? 0 : (BN == 64 ? 1 : 2);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev < 0 || dev >= 64 || configured_smem[dev][slot] < static_cast<int>(smem)) {
+      GNN_CUDA_TRY(cudaFuncSetAttribute(gemm_tf32_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(smem)),
+                   "gemm_tf32_tc_kernel: shared memory opt-in");
+      if (dev >= 0 && dev < 64) configured_smem[dev][slot] = static_cast<int>(smem);
+    }
+  }
+  TcParams p{};
+  p.m = m;
+  p.k = k;
+  p.n = n;
+  p.m_tiles = (m + BM - 1) / BM;
+  p.n_tiles = static_cast<int>(n / BN);
+  p.bias = bias;
+  p.out = out;
+  p.relu = relu ? 1 : 0;
+  const int64_t tiles = p.m_tiles * p.n_tiles;
+  int64_t ctas = std::min<int64_t>(tiles, sm_count());
+  ctas = std::max<int64_t>(p.n_tiles, (ctas / p.n_tiles) * p.n_tiles);
+  gemm_tf32_tc_kernel<BN><<<static_cast<unsigned>(ctas), kThreads, smem, stream>>>(tx, w, p);
+  GNN_LAUNCH_CHECK("gemm_tf32_tc_kernel launch");
+  return GNN_OK;
+}
+
+}  // namespace
+
+bool gemm_tc_eligible(const float* x, const float* w, const float* bias, const float* out, int64_t m, int64_t k,
+                      int64_t n) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) |
+                      reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(bias);
+  return shape_ok(m, k, n) && (a % 16 == 0) && device_is_sm100() && encode_fn() != nullptr &&
+         smem_bytes(pick_bn(n), k) <= 227 * 1024;
+}
+
+int gemm_tc_tf32(const float* x, const float* w, const float* bias, float* out, int64_t m, int64_t k, int64_t n,
+                 bool relu, cudaStream_t stream, bool* handled) {
   *handled = false;
+  if (!gemm_tc_eligible(x, w, bias, out, m, k, n)) return GNN_OK;
+  int rc;
+  switch (pick_bn(n)) {
+    case 128: rc = launch_bn<128>(x, w, bias, out, m, k, n, relu, stream); break;
+    case 64: rc = launch_bn<64>(x, w, bias, out, m, k, n, relu, stream); break;
+    default: rc = launch_bn<32>(x, w, bias, out, m, k, n, relu, stream); break;
+  }
+  if (rc == GNN_OK) *handled = true;
+  return rc;
+}
+
+int tc_status_read(int reset, int* status) {
+  GNN_CUDA_TRY(cudaMemcpyFromSymbol(status, g_tc_status, sizeof(int)), "read tensor-core status word");
+  if (reset) {
+    const int zero = 0;
+    GNN_CUDA_TRY(cudaMemcpyToSymbol(g_tc_status, &zero, sizeof(int)), "reset tensor-core status word");
+  }
   return GNN_OK;
 }
 
 }  // namespace gnnb200
 
+extern "C" int gnn_device_status(int reset, int* status) {
+  GNN_REQUIRE(status != nullptr, GNN_ERR_NULL_POINTER, "status must not be NULL");
+  const int rc = gnnb200::tc_status_read(reset, status);
+  if (rc == GNN_OK) gnnb200::clear_error();
+  return rc;
+}
+
 extern "C" int gnn_gemm_uses_tensor_cores(int64_t m, int64_t k, int64_t n) {
-  (void)m; (void)k; (void)n;
-  return 0;
+  return (gnnb200::shape_ok(m, k, n) && gnnb200::device_is_sm100() && gnnb200::encode_fn() != nullptr) ? 1 : 0;
 }

@@ -74,8 +74,15 @@ int gnn_config_get_int(const char* name, int64_t* value);
 /* Number of kernels this library has launched in this process (all devices). */
 uint64_t gnn_kernel_launches(void);
 /* 1 when GNN_PRECISION_TF32 GEMMs of this shape run on the tcgen05 tensor
- * cores of the current device, 0 when they run on the FFMA kernel. */
+ * cores of the current device, 0 when they run on the FFMA kernel
+ * (eligible: 32 <= K <= 256, K % 32 == 0, N % 128 == 0 or N in {32, 64},
+ * 16-byte aligned operands). */
 int gnn_gemm_uses_tensor_cores(int64_t m, int64_t k, int64_t n);
+/* Device-side bounded waits (mbarrier spins in the tensor-core kernels) give up
+ * after ~2 s instead of hanging; they then record a non-zero code here and the
+ * kernel returns early. Synchronises with the current device, stores the word
+ * in *status and clears it when reset != 0. */
+int gnn_device_status(int reset, int* status);
 
 /* ---- CSR aggregation (SpMM) ------------------------------------------------
  * All aggregation entry points compute, for every row r of a dst-major CSR,

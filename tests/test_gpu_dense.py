@@ -47,6 +47,30 @@ def test_linear_tf32_within_tolerance(m, k, n, relu):
     assert np.all(err <= 2e-3 * scale + 1e-30), float(np.max(err / (scale + 1e-30)))
 
 
+TC_SHAPES = [(100_000, 128, 128), (70_000, 256, 256), (5000, 128, 64), (5000, 64, 32), (257, 32, 128),
+             (130, 128, 256), (1, 128, 128), (128 * 148 * 3 + 5, 128, 128)]
+
+
+@pytest.mark.parametrize("m,k,n", TC_SHAPES)
+def test_tensor_core_gemm_shapes(m, k, n):
+    """Shapes routed to the tcgen05 kernel: TF32 tolerance, and no bounded wait gave up."""
+    assert N.lib().gnn_gemm_uses_tensor_cores(m, k, n) == 1
+    x, w, b = _rand((m, k), 21), _rand((k, n), 22), _rand((n,), 23)
+    out = torch.full((m, n), float("nan"), device=DEV)
+    native_ops.linear_forward_(x.to(DEV), w.to(DEV), b.to(DEV), out, True, precision=N.GNN_PRECISION_TF32)
+    import ctypes
+    status = ctypes.c_int(-1)
+    N.check(N.lib().gnn_device_status(1, ctypes.byref(status)))
+    assert status.value == 0
+    got = out.cpu().numpy().astype(np.float64)
+    ref = x.numpy().astype(np.float64) @ w.numpy().astype(np.float64) + b.numpy()[None, :]
+    ref = np.maximum(ref, 0.0)
+    scale = np.abs(x.numpy()).astype(np.float64) @ np.abs(w.numpy()).astype(np.float64) + np.abs(b.numpy())[None, :]
+    assert np.all(np.abs(got - ref) <= 2e-3 * scale + 1e-30)
+    # and it really is TF32, not FP32: the error is above FP32 rounding somewhere
+    assert np.max(np.abs(got - ref) / (scale + 1e-30)) > 1e-6
+
+
 def test_linear_fp32_bit_exact_with_bias_relu():
     x, w, b = _rand((777, 128), 6), _rand((128, 96), 7), _rand((96,), 8)
     out = torch.empty(777, 96, device=DEV)
