@@ -77,6 +77,9 @@ extern "C" int gnn_config_set_int(const char* name, int64_t value) {
     GNN_REQUIRE(value >= 4 && value <= 16, GNN_ERR_INVALID_ARGUMENT,
                 "spmm.long_row_warps must be in [4, 16]");
     config().long_row_warps.store(value);
+  } else if (std::strcmp(name, "spmm.kernel") == 0) {
+    GNN_REQUIRE(value == 0 || value == 1, GNN_ERR_INVALID_ARGUMENT, "spmm.kernel must be 0 or 1");
+    config().spmm_kernel.store(value);
   } else {
     return fail(GNN_ERR_INVALID_ARGUMENT, std::string("unknown config key: ") + name);
   }
@@ -90,6 +93,8 @@ extern "C" int gnn_config_get_int(const char* name, int64_t* value) {
     *value = config().long_row_threshold.load();
   } else if (std::strcmp(name, "spmm.long_row_warps") == 0) {
     *value = config().long_row_warps.load();
+  } else if (std::strcmp(name, "spmm.kernel") == 0) {
+    *value = config().spmm_kernel.load();
   } else {
     return fail(GNN_ERR_INVALID_ARGUMENT, std::string("unknown config key: ") + name);
   }

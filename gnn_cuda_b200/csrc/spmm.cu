@@ -39,8 +39,10 @@ constexpr unsigned kFull = 0xffffffffu;
 constexpr int kBlockThreads = 512;       // 16 warps
 constexpr int kRowsPerWarp = 4;          // rows a warp takes per normal block
 constexpr int kTileF4 = 128;             // float4 columns per feature tile (512 floats)
-constexpr int kMaxTiles = 62;            // per-tile tickets live in the workspace header
-constexpr size_t kWsHeader = 256;        // counters: [0] long-row count, [2+t] ticket of tile t
+constexpr int kMaxTiles = 30;            // per-tile tickets live in the workspace header
+constexpr size_t kWsHeader = 256;        // uint32 counters, see below
+constexpr int kLongTicket = 2;           // [0] long-row count, [2+t] long-row ticket of tile t
+constexpr int kItemTicket = 32;          // [32+t] work-item ticket of tile t
 constexpr int64_t kMinLongThreshold = 32;
 
 enum WeightMode : int { kUnit = 0, kGcn = 1, kEdge = 2 };
@@ -251,6 +253,196 @@ __global__ void __launch_bounds__(kBlockThreads, 2)
   }
 }
 
+// Persistent packed-stream kernel (the default vector path).
+//
+// Phase 1 — whole blocks take long rows from the plan list (atomic ticket) and
+// split each over all warps, partials added in warp order (same as above).
+// Phase 2 — every warp independently takes work items of 32 consecutive row
+// slots (atomic ticket). For an item it prefix-sums the 32 row degrees (long
+// rows count as 0) and walks the item's edges as one packed stream in batches
+// of 32: lane l handles stream position v0 + l, finds its row by a 5-step
+// shuffle binary search over the prefix sums, and loads that edge's column
+// (and weight) — coalesced, because consecutive positions are consecutive CSR
+// entries. The warp then gathers the batch's neighbour rows U at a time and
+// accumulates them in stream order, writing each row when the stream moves
+// past it. Every short row is still summed edge by edge in CSR order by one
+// warp, so results are identical to the per-row kernel; what changes is that
+// low-degree rows no longer leave lanes idle or serialise a row_ptr -> col ->
+// gather latency chain per row, and no warp waits for slower rows of its block.
+template <int WM, int MEAN, bool HOT, int NV, class IdxT>
+__global__ void __launch_bounds__(kBlockThreads, 2) spmm_stream_kernel(SpmmArgs a) {
+  constexpr int U = (NV == 1) ? 8 : (NV == 2 ? 4 : 2);
+  extern __shared__ float4 s_part[];  // [nwarps][32 * NV] (long rows only)
+  __shared__ uint32_t s_ticket;
+
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int nwarps = blockDim.x >> 5;
+  const int tile = blockIdx.y;
+  const int64_t f4 = a.f >> 2;
+  const int64_t col0 = static_cast<int64_t>(tile) * kTileF4 + lane;
+  bool valid[NV];
+#pragma unroll
+  for (int q = 0; q < NV; ++q) valid[q] = (col0 + 32 * q) < f4;
+  const IdxT* __restrict__ rp = static_cast<const IdxT*>(a.row_ptr);
+
+  // ---------------- phase 1: long rows ----------------
+  if (a.long_cap > 0) {
+    const uint32_t count = min(__ldcg(&a.counters[0]), static_cast<uint32_t>(a.long_cap));
+    while (true) {
+      if (threadIdx.x == 0) s_ticket = atomicAdd(&a.counters[kLongTicket + tile], 1u);
+      __syncthreads();
+      const uint32_t t = s_ticket;
+      __syncthreads();
+      if (t >= count) break;
+      const int64_t r = a.long_list[t];
+      const IdxT beg = rp[r];
+      const IdxT end = rp[r + 1];
+      const int64_t deg = static_cast<int64_t>(end - beg);
+      const int64_t chunk = (deg + nwarps - 1) / nwarps;
+      const IdxT wb = static_cast<IdxT>(min(static_cast<int64_t>(beg) + warp * chunk, static_cast<int64_t>(end)));
+      const IdxT we = static_cast<IdxT>(min(static_cast<int64_t>(wb) + chunk, static_cast<int64_t>(end)));
+      const float rs = (WM == kGcn) ? __ldg(a.dis_row + r) : 1.0f;
+      float4 acc[NV];
+#pragma unroll
+      for (int q = 0; q < NV; ++q) acc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+      accumulate_edges<WM, HOT, NV, U, IdxT>(a, wb, we, rs, lane, col0, valid, acc);
+#pragma unroll
+      for (int q = 0; q < NV; ++q) s_part[warp * 32 * NV + q * 32 + lane] = acc[q];
+      __syncthreads();
+      for (int j = threadIdx.x; j < 32 * NV; j += blockDim.x) {
+        const int64_t cj = static_cast<int64_t>(tile) * kTileF4 + j;
+        if (cj < f4) {
+          float4 s = s_part[j];
+          for (int w = 1; w < nwarps; ++w) s = add4(s, s_part[w * 32 * NV + j]);
+          s = finish<MEAN>(s, deg);
+          reinterpret_cast<float4*>(a.out + r * a.f)[cj] = s;
+        }
+      }
+      __syncthreads();
+    }
+  }
+
+  // ---------------- phase 2: packed streams of short rows ----------------
+  const int64_t items = (a.n + 31) >> 5;
+  while (true) {
+    uint32_t item = 0;
+    if (lane == 0) item = atomicAdd(&a.counters[kItemTicket + tile], 1u);
+    item = __shfl_sync(kFull, item, 0);
+    if (static_cast<int64_t>(item) >= items) break;
+    const int64_t s0 = static_cast<int64_t>(item) << 5;
+
+    // this lane's row of the item
+    int64_t row = 0;
+    IdxT rbeg = 0;
+    int deg = 0;        // degree counted in the stream (0 for long rows)
+    int true_deg = 0;   // for the mean
+    bool live = false;  // a row this warp must write
+    float rs = 1.0f;
+    if (s0 + lane < a.n) {
+      row = a.sched ? a.sched[s0 + lane] : s0 + lane;
+      rbeg = rp[row];
+      const int64_t d = static_cast<int64_t>(rp[row + 1]) - static_cast<int64_t>(rbeg);
+      live = d <= a.long_thr;
+      deg = live ? static_cast<int>(d) : 0;
+      true_deg = deg;
+      if (WM == kGcn) rs = __ldg(a.dis_row + row);
+    }
+    // exclusive prefix sum of the stream degrees
+    int off = deg;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int t = __shfl_up_sync(kFull, off, d);
+      if (lane >= d) off += t;
+    }
+    const int total = __shfl_sync(kFull, off, 31);
+    off -= deg;
+
+    float4 acc[NV];
+#pragma unroll
+    for (int q = 0; q < NV; ++q) acc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+    int cur = 0;  // item-local row being accumulated
+
+    // writes row `cur` (if this warp owns it) and clears the accumulator
+    auto flush = [&]() {
+      const int64_t orow_id = __shfl_sync(kFull, row, cur);
+      const int is_live = __shfl_sync(kFull, static_cast<int>(live), cur);
+      const int d = __shfl_sync(kFull, true_deg, cur);
+      if (is_live) {
+        float4* orow = reinterpret_cast<float4*>(a.out + orow_id * a.f);
+#pragma unroll
+        for (int q = 0; q < NV; ++q) {
+          if (valid[q]) orow[col0 + 32 * q] = finish<MEAN>(acc[q], d);
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < NV; ++q) acc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+    };
+
+    for (int v0 = 0; v0 < total; v0 += 32) {
+      const int cnt = min(32, total - v0);
+      // stream position v -> item row (largest i with off_i <= v)
+      const int v = v0 + lane;
+      int ri = 0;
+#pragma unroll
+      for (int step = 16; step >= 1; step >>= 1) {
+        const int oc = __shfl_sync(kFull, off, ri + step);
+        if (oc <= v) ri += step;
+      }
+      const IdxT rb_i = __shfl_sync(kFull, rbeg, ri);
+      const int off_i = __shfl_sync(kFull, off, ri);
+      const float rs_i = __shfl_sync(kFull, rs, ri);
+      int c = 0;
+      float w = 0.0f;
+      if (lane < cnt) {
+        const IdxT e = rb_i + static_cast<IdxT>(v - off_i);
+        c = ld_stream_i32(a.col + e);
+        w = edge_weight<WM>(a, rs_i, c, static_cast<int64_t>(e));
+      }
+      for (int j = 0; j < cnt; j += U) {
+        float4 vals[U][NV];
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+          const int ck = __shfl_sync(kFull, c, (j + k) & 31);
+          if (j + k < cnt) {
+            const float4* xr = reinterpret_cast<const float4*>(feature_row<HOT>(a, ck));
+#pragma unroll
+            for (int q = 0; q < NV; ++q) {
+              if (valid[q]) vals[k][q] = ldg_f4(xr + col0 + 32 * q);
+            }
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+          const int rk = __shfl_sync(kFull, ri, (j + k) & 31);
+          const float wk = __shfl_sync(kFull, w, (j + k) & 31);
+          if (j + k < cnt) {
+            while (cur < rk) {  // the stream moved past row `cur`
+              flush();
+              ++cur;
+            }
+#pragma unroll
+            for (int q = 0; q < NV; ++q) {
+              if (valid[q]) {
+                if constexpr (WM == kUnit) {
+                  acc[q] = add4(acc[q], vals[k][q]);
+                } else {
+                  acc[q] = fma4(wk, vals[k][q], acc[q]);
+                }
+              }
+            }
+          }
+        }
+      }
+    }
+    // rows after the last edge of the item (and the last row itself)
+    while (cur < 32 && s0 + cur < a.n) {
+      flush();
+      ++cur;
+    }
+  }
+}
+
 // Scalar kernel for feature widths that are not a multiple of 4 (or unaligned
 // pointers): one warp per row, lane l owns features l, l+32, l+64, l+96 of the
 // block's 128-feature tile; plain CSR order for every row.
@@ -331,18 +523,37 @@ int launch_vec(SpmmArgs a, cudaStream_t stream) {
   const int64_t rows_per_block = static_cast<int64_t>(nwarps) * kRowsPerWarp;
   const int64_t normal_blocks = (a.n + rows_per_block - 1) / rows_per_block;
 
-  int num_long_blocks = 0;
-  if (a.long_cap > 0 && a.counters != nullptr) {
-    num_long_blocks = static_cast<int>(std::min<int64_t>(a.long_cap, 2 * sm_count()));
-  }
-  const int64_t gx = normal_blocks + num_long_blocks;
-  if (gx > 0x7fffffffLL) return fail(GNN_ERR_UNSUPPORTED, "spmm: too many rows for one launch");
-  dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(tiles));
-  dim3 block(threads);
   const size_t smem = static_cast<size_t>(nwarps) * 32 * nv * sizeof(float4);
+  dim3 block(threads);
 
-#define GNN_LAUNCH_NV(NVV)                                                                   \
+  if (config().spmm_kernel.load() == 1) {
+    // per-row kernel: one warp per row, blocks of consecutive rows
+    int num_long_blocks = 0;
+    if (a.long_cap > 0) num_long_blocks = static_cast<int>(std::min<int64_t>(a.long_cap, 2 * sm_count()));
+    const int64_t gx = normal_blocks + num_long_blocks;
+    if (gx > 0x7fffffffLL) return fail(GNN_ERR_UNSUPPORTED, "spmm: too many rows for one launch");
+    dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(tiles));
+#define GNN_LAUNCH_NV(NVV) \
   spmm_vec_kernel<WM, MEAN, HOT, NVV, IdxT><<<grid, block, smem, stream>>>(a, num_long_blocks)
+    switch (nv) {
+      case 1: GNN_LAUNCH_NV(1); break;
+      case 2: GNN_LAUNCH_NV(2); break;
+      case 3: GNN_LAUNCH_NV(3); break;
+      default: GNN_LAUNCH_NV(4); break;
+    }
+#undef GNN_LAUNCH_NV
+    GNN_LAUNCH_CHECK("spmm kernel launch");
+    return GNN_OK;
+  }
+
+  // persistent packed-stream kernel: as many blocks as are resident at once
+  // (2 per SM at 64 registers x 512 threads), fewer for small graphs
+  const int64_t items = (a.n + 31) / 32;
+  const int64_t resident = 2LL * sm_count();
+  int64_t gx = std::max<int64_t>((items + nwarps - 1) / nwarps, a.long_cap > 0 ? std::min(a.long_cap, resident) : 1);
+  gx = std::max<int64_t>(1, std::min(gx, resident));
+  dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(tiles));
+#define GNN_LAUNCH_NV(NVV) spmm_stream_kernel<WM, MEAN, HOT, NVV, IdxT><<<grid, block, smem, stream>>>(a)
   switch (nv) {
     case 1: GNN_LAUNCH_NV(1); break;
     case 2: GNN_LAUNCH_NV(2); break;
@@ -410,16 +621,18 @@ int run_typed(const SpmmRequest& q, cudaStream_t stream) {
     return fail(GNN_ERR_UNSUPPORTED, "spmm: feat_dim above " + std::to_string(kMaxTiles * 512) +
                                          " is not supported");
   }
-  a.long_thr = resolve_long_threshold(q.n, q.nnz);
+  // Stream degrees are summed in 32-bit over 32 rows, so the threshold is capped at 2^25.
+  a.long_thr = std::min<int64_t>(resolve_long_threshold(q.n, q.nnz), int64_t(1) << 25);
   a.long_cap = std::min<int64_t>(long_capacity(q.n, q.nnz), q.nnz / (a.long_thr + 1) + 1);
   if (q.nnz <= a.long_thr) a.long_cap = 0;  // no row can be long
+  // the workspace holds the work tickets (and the long-row list when needed)
+  if (q.ws == nullptr || q.ws_bytes < gnn_spmm_workspace_bytes(q.n, q.nnz)) {
+    return fail(GNN_ERR_WORKSPACE, "spmm: workspace missing or smaller than gnn_spmm_workspace_bytes()");
+  }
+  a.counters = static_cast<uint32_t*>(q.ws);
+  a.long_list = reinterpret_cast<uint32_t*>(static_cast<char*>(q.ws) + kWsHeader);
+  GNN_CUDA_TRY(cudaMemsetAsync(q.ws, 0, kWsHeader, stream), "spmm: workspace reset");
   if (a.long_cap > 0) {
-    if (q.ws == nullptr || q.ws_bytes < gnn_spmm_workspace_bytes(q.n, q.nnz)) {
-      return fail(GNN_ERR_WORKSPACE, "spmm: workspace missing or smaller than gnn_spmm_workspace_bytes()");
-    }
-    a.counters = static_cast<uint32_t*>(q.ws);
-    a.long_list = reinterpret_cast<uint32_t*>(static_cast<char*>(q.ws) + kWsHeader);
-    GNN_CUDA_TRY(cudaMemsetAsync(q.ws, 0, kWsHeader, stream), "spmm: workspace reset");
     const int threads = 256;
     const int64_t want = (q.n + threads - 1) / threads;
     const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, 8LL * sm_count())));

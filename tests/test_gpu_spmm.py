@@ -218,6 +218,29 @@ def test_workspace_reuse_and_streams():
     assert len(native_ops._workspaces) >= 1
 
 
+@pytest.mark.parametrize("f", [128, 256, 512, 640])
+def test_stream_and_per_row_kernels_identical(f):
+    """The packed-stream kernel (default) and the one-warp-per-row kernel give the same bits."""
+    n = 5000
+    s, d = _graph("rmat", n, seed=12)
+    rp, ci, dis = O.gcn_normalized_csr(s.numpy(), d.numpy(), n)
+    x = synth.features(n, f, seed=13).numpy()
+    t = [torch.from_numpy(a).to(DEV) for a in (rp, ci, dis, x)]
+    outs = []
+    old = N.config_get("spmm.kernel")
+    try:
+        for kern in (0, 1):
+            N.config_set("spmm.kernel", kern)
+            o = torch.full((n, f), float("nan"), device=DEV)
+            gcn_ops.spmm_gcn_forward_(*t, o)
+            outs.append(o.cpu().numpy())
+    finally:
+        N.config_set("spmm.kernel", old)
+    assert _bits_equal(outs[0], outs[1])
+    exp = O.spmm(rp, ci, x, mode=O.W_GCN, dis=dis, split_warps=16, long_thr=256)
+    assert _bits_equal(outs[0], exp)
+
+
 def test_long_row_warp_counts():
     n, f = 3000, 128
     s, d = _graph("hub", n, seed=3)
