@@ -62,6 +62,13 @@ def _workspace(device: torch.device, nbytes: int) -> tuple[int, int]:
     return buf.data_ptr(), buf.numel()
 
 
+def ensure_workspace(device: torch.device, num_nodes: int, num_edges: int) -> None:
+    """Allocate the aggregation workspace of the current stream now (e.g. before a
+    caller reserves the rest of device memory), so later calls allocate nothing."""
+    with torch.cuda.device(device):
+        _workspace(device, N.lib().gnn_spmm_workspace_bytes(int(num_nodes), int(num_edges)))
+
+
 def _index_type(row_ptr: torch.Tensor) -> int:
     if row_ptr.dtype == torch.int32:
         return N.GNN_INDEX_INT32
