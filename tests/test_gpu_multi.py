@@ -1,0 +1,96 @@
+"""Row-partitioned multi-GPU GCN forward (NCCL) equals the single-GPU forward bit for bit.
+
+Runs only where at least two GPUs are visible (spawned ranks, one GPU each,
+NCCL with NVLS off). The long-row threshold is fixed so every rank uses the
+same per-row schedule as the single-GPU run.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+N_NODES, FEAT, LAYERS, THR = 20000, 128, 2, 64
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _problem(device):
+    from gnn_cuda_b200 import synth
+    u, v = synth.rmat_undirected(N_NODES, N_NODES * 12, seed=61)
+    s, d = synth.symmetrize(u, v)
+    rp, ci, dis = synth.csr_on_device(s.to(device), d.to(device), N_NODES, add_self_loops=True)
+    x = synth.features(N_NODES, FEAT, seed=62).to(device)
+    ws = [synth.glorot(FEAT, FEAT, seed=63 + i).to(device) for i in range(LAYERS)]
+    bs = [torch.full((FEAT,), 0.01 * (i + 1), device=device) for i in range(LAYERS)]
+    return rp, ci, dis, x, ws, bs
+
+
+def _worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import datetime
+    import torch.distributed as dist
+    from gnn_cuda_b200 import _native as N
+    from gnn_cuda_b200 import partition
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    try:
+        N.config_set("spmm.long_row_threshold", THR)
+        torch.backends.cuda.matmul.allow_tf32 = True
+        rp, ci, dis, x, ws, bs = _problem(dev)
+        bounds = partition.nnz_balanced_bounds(rp.cpu().numpy(), world)
+        shard = partition.make_shard(rp, ci, bounds[rank], bounds[rank + 1])
+        rows = shard.num_rows
+        bufs = {k: torch.empty(rows, FEAT, device=dev) for k in ("agg", "out0", "out1")}
+        bufs["x_next"] = torch.empty(N_NODES, FEAT, device=dev)
+        out = partition.gcn_forward_partitioned(shard, dis, x, ws, bs, bounds, rank, bufs)
+        full = torch.empty(N_NODES, FEAT, device=dev)
+        partition.exchange_rows(out, full, bounds, rank)
+        torch.cuda.synchronize(dev)
+        q.put((rank, full.cpu().numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_gpu_partitioned_gcn_matches_single_gpu():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    from gnn_cuda_b200 import _native as N
+    from gnn_cuda_b200.GNN_cuda_common import agg_ops, gcn_ops
+    dev = torch.device("cuda", 0)
+    old = N.config_get("spmm.long_row_threshold")
+    N.config_set("spmm.long_row_threshold", THR)
+    try:
+        torch.backends.cuda.matmul.allow_tf32 = True
+        rp, ci, dis, x, ws, bs = _problem(dev)
+        agg = torch.empty(N_NODES, FEAT, device=dev)
+        h = x
+        for li in range(LAYERS):
+            gcn_ops.spmm_gcn_forward_(rp, ci, dis, h, agg)
+            o = torch.empty(N_NODES, FEAT, device=dev)
+            agg_ops.linear_forward_(agg, ws[li], bs[li], o, li != LAYERS - 1)
+            h = o
+        single = h.cpu().numpy()
+    finally:
+        N.config_set("spmm.long_row_threshold", old)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=300) for _ in range(2))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for r in range(2):
+        assert np.array_equal(results[r].view(np.uint32), single.view(np.uint32)), r
