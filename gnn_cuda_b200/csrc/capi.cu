@@ -78,7 +78,7 @@ extern "C" int gnn_config_set_int(const char* name, int64_t value) {
                 "spmm.long_row_warps must be in [4, 16]");
     config().long_row_warps.store(value);
   } else if (std::strcmp(name, "spmm.kernel") == 0) {
-    GNN_REQUIRE(value == 0 || value == 1, GNN_ERR_INVALID_ARGUMENT, "spmm.kernel must be 0 or 1");
+    GNN_REQUIRE(value >= 0 && value <= 2, GNN_ERR_INVALID_ARGUMENT, "spmm.kernel must be 0, 1 or 2");
     config().spmm_kernel.store(value);
   } else {
     return fail(GNN_ERR_INVALID_ARGUMENT, std::string("unknown config key: ") + name);

@@ -55,7 +55,7 @@ void count_launch();
 struct Config {
   std::atomic<int64_t> long_row_threshold{0};  // 0 = automatic
   std::atomic<int64_t> long_row_warps{16};
-  std::atomic<int64_t> spmm_kernel{0};  // 0 packed-stream (default), 1 one-warp-per-row
+  std::atomic<int64_t> spmm_kernel{1};  // 0 packed stream, 1 one warp per row (default), 2 cp.async staging
 };
 Config& config();
 

@@ -37,13 +37,37 @@ namespace {
 
 constexpr unsigned kFull = 0xffffffffu;
 constexpr int kBlockThreads = 512;       // 16 warps
-constexpr int kRowsPerWarp = 4;          // rows a warp takes per normal block
+#ifndef GNN_SPMM_ROWS_PER_WARP
+#define GNN_SPMM_ROWS_PER_WARP 4
+#endif
+constexpr int kRowsPerWarp = GNN_SPMM_ROWS_PER_WARP;  // rows a warp takes per block (<= 32)
 constexpr int kTileF4 = 128;             // float4 columns per feature tile (512 floats)
 constexpr int kMaxTiles = 30;            // per-tile tickets live in the workspace header
 constexpr size_t kWsHeader = 256;        // uint32 counters, see below
 constexpr int kLongTicket = 2;           // [0] long-row count, [2+t] long-row ticket of tile t
 constexpr int kItemTicket = 32;          // [32+t] work-item ticket of tile t
 constexpr int64_t kMinLongThreshold = 32;
+
+// Neighbour rows a warp gathers per round (rows in flight per warp) and the
+// number of 512-thread blocks kept resident per SM. Measured on B200: a few
+// rows in flight per warp across many warps beats deep per-warp unrolling —
+// too many outstanding gathers per SM congest the memory path.
+#ifndef GNN_SPMM_U_NV1
+#define GNN_SPMM_U_NV1 4
+#endif
+#ifndef GNN_SPMM_U_NV2
+#define GNN_SPMM_U_NV2 2
+#endif
+#ifndef GNN_SPMM_U_NV34
+#define GNN_SPMM_U_NV34 2
+#endif
+#ifndef GNN_SPMM_MIN_BLOCKS
+#define GNN_SPMM_MIN_BLOCKS 3
+#endif
+template <int NV>
+__host__ __device__ constexpr int gather_depth() {
+  return NV == 1 ? GNN_SPMM_U_NV1 : (NV == 2 ? GNN_SPMM_U_NV2 : GNN_SPMM_U_NV34);
+}
 
 enum WeightMode : int { kUnit = 0, kGcn = 1, kEdge = 2 };
 enum MeanMode : int { kNoMean = 0, kMeanDiv = 1, kMeanRcp = 2 };
@@ -65,6 +89,7 @@ struct SpmmArgs {
   uint32_t* counters;
   uint32_t* long_list;
   int64_t long_cap;
+  int long_split;          // chunks per long row (spmm.long_row_warps)
 };
 
 template <int WM>
@@ -87,17 +112,23 @@ __device__ __forceinline__ const float* feature_row(const SpmmArgs& a, int c) {
 }
 
 // Accumulates edges [beg, end) of one row into acc, edge by edge in CSR order.
-// All 32 lanes of the warp must call this with the same arguments.
+// All 32 lanes of the warp must call this with the same arguments. When
+// `have_first` is set, (c_first, w_first) already hold the first 32-edge chunk's
+// column and weight for this lane (prefetched by the caller).
 template <int WM, bool HOT, int NV, int U, class IdxT>
 __device__ __forceinline__ void accumulate_edges(const SpmmArgs& a, IdxT beg, IdxT end, float rs,
                                                  int lane, int64_t col0, const bool (&valid)[NV],
-                                                 float4 (&acc)[NV]) {
+                                                 float4 (&acc)[NV], bool have_first = false,
+                                                 int c_first = 0, float w_first = 0.0f) {
   static_assert(32 % U == 0, "U must divide the warp size");
   for (IdxT base = beg; base < end; base += 32) {
     const int cnt = static_cast<int>(min(static_cast<IdxT>(32), static_cast<IdxT>(end - base)));
     int c = 0;
     float w = 0.0f;
-    if (lane < cnt) {
+    if (have_first && base == beg) {
+      c = c_first;
+      w = w_first;
+    } else if (lane < cnt) {
       c = ld_stream_i32(a.col + base + lane);
       w = edge_weight<WM>(a, rs, c, static_cast<int64_t>(base) + lane);
     }
@@ -175,9 +206,9 @@ __global__ void plan_long_rows_kernel(const IdxT* __restrict__ row_ptr, int64_t 
 // Main vector kernel. Blocks [0, num_long_blocks) serve the long-row list;
 // the rest take kRowsPerWarp rows per warp, skipping long rows.
 template <int WM, int MEAN, bool HOT, int NV, class IdxT>
-__global__ void __launch_bounds__(kBlockThreads, 2)
+__global__ void __launch_bounds__(kBlockThreads, GNN_SPMM_MIN_BLOCKS)
     spmm_vec_kernel(SpmmArgs a, int num_long_blocks) {
-  constexpr int U = (NV == 1) ? 8 : (NV == 2 ? 4 : 2);
+  constexpr int U = gather_depth<NV>();
   extern __shared__ float4 s_part[];  // [nwarps][32 * NV] (long rows only)
   __shared__ uint32_t s_ticket;
 
@@ -231,20 +262,54 @@ __global__ void __launch_bounds__(kBlockThreads, 2)
   }
 
   // ---- normal rows ----
+  // Lane i (< kRowsPerWarp) fetches row i's bounds and scale once; the first
+  // 32-edge chunk (columns + weights) of row i+1 is loaded while row i's
+  // neighbour rows are being gathered, so a row does not start with a
+  // row_ptr -> col_ind -> gather chain of dependent loads.
   const int64_t blk = static_cast<int64_t>(blockIdx.x) - num_long_blocks;
+  int64_t my_row = -1;
+  IdxT my_beg = 0, my_end = 0;
+  float my_rs = 1.0f;
+  if (lane < kRowsPerWarp) {
+    const int64_t slot = (blk * kRowsPerWarp + lane) * nwarps + warp;
+    if (slot < a.n) {
+      my_row = a.sched ? a.sched[slot] : slot;
+      my_beg = rp[my_row];
+      my_end = rp[my_row + 1];
+      if (WM == kGcn) my_rs = __ldg(a.dis_row + my_row);
+    }
+  }
+  // first chunk of row i for this lane (no load for long rows: they are skipped)
+  auto first_chunk = [&](int i, int& c, float& w) {
+    const IdxT beg = __shfl_sync(kFull, my_beg, i);
+    const IdxT end = __shfl_sync(kFull, my_end, i);
+    const float rs = __shfl_sync(kFull, my_rs, i);
+    const int64_t deg = static_cast<int64_t>(end - beg);
+    c = 0;
+    w = 0.0f;
+    if (deg <= a.long_thr && lane < deg) {
+      c = ld_stream_i32(a.col + beg + lane);
+      w = edge_weight<WM>(a, rs, c, static_cast<int64_t>(beg) + lane);
+    }
+  };
+  int c_next = 0;
+  float w_next = 0.0f;
+  first_chunk(0, c_next, w_next);
   for (int i = 0; i < kRowsPerWarp; ++i) {
-    const int64_t slot = (blk * kRowsPerWarp + i) * nwarps + warp;
-    if (slot >= a.n) break;
-    const int64_t r = a.sched ? a.sched[slot] : slot;
-    const IdxT beg = rp[r];
-    const IdxT end = rp[r + 1];
+    const int64_t r = __shfl_sync(kFull, my_row, i);
+    if (r < 0) break;
+    const IdxT beg = __shfl_sync(kFull, my_beg, i);
+    const IdxT end = __shfl_sync(kFull, my_end, i);
+    const float rs = __shfl_sync(kFull, my_rs, i);
+    const int c_cur = c_next;
+    const float w_cur = w_next;
+    if (i + 1 < kRowsPerWarp) first_chunk(i + 1, c_next, w_next);
     const int64_t deg = static_cast<int64_t>(end - beg);
     if (deg > a.long_thr) continue;  // owned by a long-row CTA
-    const float rs = (WM == kGcn) ? __ldg(a.dis_row + r) : 1.0f;
     float4 acc[NV];
 #pragma unroll
     for (int q = 0; q < NV; ++q) acc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
-    accumulate_edges<WM, HOT, NV, U, IdxT>(a, beg, end, rs, lane, col0, valid, acc);
+    accumulate_edges<WM, HOT, NV, U, IdxT>(a, beg, end, rs, lane, col0, valid, acc, true, c_cur, w_cur);
     float4* orow = reinterpret_cast<float4*>(a.out + r * a.f);
 #pragma unroll
     for (int q = 0; q < NV; ++q) {
@@ -270,8 +335,8 @@ __global__ void __launch_bounds__(kBlockThreads, 2)
 // low-degree rows no longer leave lanes idle or serialise a row_ptr -> col ->
 // gather latency chain per row, and no warp waits for slower rows of its block.
 template <int WM, int MEAN, bool HOT, int NV, class IdxT>
-__global__ void __launch_bounds__(kBlockThreads, 2) spmm_stream_kernel(SpmmArgs a) {
-  constexpr int U = (NV == 1) ? 8 : (NV == 2 ? 4 : 2);
+__global__ void __launch_bounds__(kBlockThreads, GNN_SPMM_MIN_BLOCKS) spmm_stream_kernel(SpmmArgs a) {
+  constexpr int U = gather_depth<NV>();
   extern __shared__ float4 s_part[];  // [nwarps][32 * NV] (long rows only)
   __shared__ uint32_t s_ticket;
 
@@ -443,6 +508,232 @@ __global__ void __launch_bounds__(kBlockThreads, 2) spmm_stream_kernel(SpmmArgs 
   }
 }
 
+// ---------------------------------------------------------------------------
+// Asynchronous-staging variant of the packed-stream kernel.
+//
+// Same work decomposition and per-row arithmetic as spmm_stream_kernel, but the
+// neighbour rows are not gathered into registers: each lane copies its 16-byte
+// slices of a batch of kAsyncBatch rows straight into a per-warp shared-memory
+// ring with cp.async (L1-bypassing), commits the batch, and only then consumes
+// the previous batch from shared memory. Two batches are in flight per warp
+// while it computes, and no registers are tied up by outstanding loads, so
+// bytes in flight per SM are bounded by shared memory (~190 KB) instead of by
+// the register file. Every lane reads back only the bytes it copied itself, so
+// per-thread cp.async.wait_group is the only synchronisation needed.
+// ---------------------------------------------------------------------------
+constexpr int kAsyncBatch = 16;   // edges per stage
+constexpr int kAsyncStages = 2;
+
+__device__ __forceinline__ void cp_async16(uint32_t smem_addr, const void* gptr) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr), "l"(gptr) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <int WM, int MEAN, bool HOT, int NV, class IdxT>
+__global__ void __launch_bounds__(384, 1) spmm_async_kernel(SpmmArgs a) {
+  extern __shared__ float4 s_dyn[];
+  __shared__ uint32_t s_ticket;
+  constexpr int kRowF4 = 32 * NV;                                 // float4 slots per staged row
+  constexpr int kWarpF4 = kAsyncStages * kAsyncBatch * kRowF4;    // per-warp ring
+
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int nwarps = blockDim.x >> 5;
+  const int tile = blockIdx.y;
+  const int64_t f4 = a.f >> 2;
+  const int64_t col0 = static_cast<int64_t>(tile) * kTileF4 + lane;
+  bool valid[NV];
+#pragma unroll
+  for (int q = 0; q < NV; ++q) valid[q] = (col0 + 32 * q) < f4;
+  const IdxT* __restrict__ rp = static_cast<const IdxT*>(a.row_ptr);
+  float4* ring = s_dyn + warp * kWarpF4;  // also reused as [nwarps][32*NV] partials for long rows
+  const uint32_t ring_addr = static_cast<uint32_t>(__cvta_generic_to_shared(ring));
+
+  // ---------------- phase 1: long rows (register gathers) ----------------
+  // A long row is cut into a.long_split contiguous chunks (the same cut as the
+  // other kernels, whatever this block's warp count); warp w sums chunks
+  // w, w + nwarps, ... into their own shared-memory slots, which are then added
+  // in chunk order.
+  if (a.long_cap > 0) {
+    constexpr int U = gather_depth<NV>();
+    const int split = a.long_split;
+    const uint32_t count = min(__ldcg(&a.counters[0]), static_cast<uint32_t>(a.long_cap));
+    while (true) {
+      if (threadIdx.x == 0) s_ticket = atomicAdd(&a.counters[kLongTicket + tile], 1u);
+      __syncthreads();
+      const uint32_t t = s_ticket;
+      __syncthreads();
+      if (t >= count) break;
+      const int64_t r = a.long_list[t];
+      const IdxT beg = rp[r];
+      const IdxT end = rp[r + 1];
+      const int64_t deg = static_cast<int64_t>(end - beg);
+      const int64_t chunk = (deg + split - 1) / split;
+      const float rs = (WM == kGcn) ? __ldg(a.dis_row + r) : 1.0f;
+      for (int cidx = warp; cidx < split; cidx += nwarps) {
+        const IdxT wb = static_cast<IdxT>(min(static_cast<int64_t>(beg) + cidx * chunk, static_cast<int64_t>(end)));
+        const IdxT we = static_cast<IdxT>(min(static_cast<int64_t>(wb) + chunk, static_cast<int64_t>(end)));
+        float4 acc[NV];
+#pragma unroll
+        for (int q = 0; q < NV; ++q) acc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+        accumulate_edges<WM, HOT, NV, U, IdxT>(a, wb, we, rs, lane, col0, valid, acc);
+#pragma unroll
+        for (int q = 0; q < NV; ++q) s_dyn[cidx * 32 * NV + q * 32 + lane] = acc[q];
+      }
+      __syncthreads();
+      for (int j = threadIdx.x; j < 32 * NV; j += blockDim.x) {
+        const int64_t cj = static_cast<int64_t>(tile) * kTileF4 + j;
+        if (cj < f4) {
+          float4 s = s_dyn[j];
+          for (int w = 1; w < split; ++w) s = add4(s, s_dyn[w * 32 * NV + j]);
+          s = finish<MEAN>(s, deg);
+          reinterpret_cast<float4*>(a.out + r * a.f)[cj] = s;
+        }
+      }
+      __syncthreads();
+    }
+  }
+
+  // ---------------- phase 2: packed streams with cp.async staging ----------------
+  const int64_t items = (a.n + 31) >> 5;
+  while (true) {
+    uint32_t item = 0;
+    if (lane == 0) item = atomicAdd(&a.counters[kItemTicket + tile], 1u);
+    item = __shfl_sync(kFull, item, 0);
+    if (static_cast<int64_t>(item) >= items) break;
+    const int64_t s0 = static_cast<int64_t>(item) << 5;
+
+    int64_t row = 0;
+    IdxT rbeg = 0;
+    int deg = 0;
+    int true_deg = 0;
+    bool live = false;
+    float rs = 1.0f;
+    if (s0 + lane < a.n) {
+      row = a.sched ? a.sched[s0 + lane] : s0 + lane;
+      rbeg = rp[row];
+      const int64_t d = static_cast<int64_t>(rp[row + 1]) - static_cast<int64_t>(rbeg);
+      live = d <= a.long_thr;
+      deg = live ? static_cast<int>(d) : 0;
+      true_deg = deg;
+      if (WM == kGcn) rs = __ldg(a.dis_row + row);
+    }
+    int off = deg;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int t = __shfl_up_sync(kFull, off, d);
+      if (lane >= d) off += t;
+    }
+    const int total = __shfl_sync(kFull, off, 31);
+    off -= deg;
+
+    float4 acc[NV];
+#pragma unroll
+    for (int q = 0; q < NV; ++q) acc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+    int cur = 0;
+    auto flush = [&]() {
+      const int64_t orow_id = __shfl_sync(kFull, row, cur);
+      const int is_live = __shfl_sync(kFull, static_cast<int>(live), cur);
+      const int d = __shfl_sync(kFull, true_deg, cur);
+      if (is_live) {
+        float4* orow = reinterpret_cast<float4*>(a.out + orow_id * a.f);
+#pragma unroll
+        for (int q = 0; q < NV; ++q) {
+          if (valid[q]) orow[col0 + 32 * q] = finish<MEAN>(acc[q], d);
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < NV; ++q) acc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+    };
+
+    // previous batch, waiting in the ring: its weights / rows live in lanes 0..prev_cnt-1
+    int prev_cnt = 0;
+    int prev_ri = 0;
+    float prev_w = 0.0f;
+    int stage = 0;
+    const int nbatches = (total + kAsyncBatch - 1) / kAsyncBatch;
+    for (int b = 0; b <= nbatches; ++b) {
+      int cnt = 0;
+      int ri = 0;
+      float w = 0.0f;
+      if (b < nbatches) {
+        // ---- prepare and issue batch b ----
+        const int v0 = b * kAsyncBatch;
+        cnt = min(kAsyncBatch, total - v0);
+        const int v = v0 + lane;
+#pragma unroll
+        for (int step = 16; step >= 1; step >>= 1) {
+          const int oc = __shfl_sync(kFull, off, ri + step);
+          if (oc <= v) ri += step;
+        }
+        const IdxT rb_i = __shfl_sync(kFull, rbeg, ri);
+        const int off_i = __shfl_sync(kFull, off, ri);
+        const float rs_i = __shfl_sync(kFull, rs, ri);
+        int c = 0;
+        if (lane < cnt) {
+          const IdxT e = rb_i + static_cast<IdxT>(v - off_i);
+          c = ld_stream_i32(a.col + e);
+          w = edge_weight<WM>(a, rs_i, c, static_cast<int64_t>(e));
+        }
+        const uint32_t stage_addr = ring_addr + static_cast<uint32_t>(stage * kAsyncBatch * kRowF4 * 16);
+        for (int j = 0; j < cnt; ++j) {
+          const int cj = __shfl_sync(kFull, c, j);
+          const float* xr = feature_row<HOT>(a, cj);
+#pragma unroll
+          for (int q = 0; q < NV; ++q) {
+            if (valid[q]) {
+              cp_async16(stage_addr + static_cast<uint32_t>((j * kRowF4 + q * 32 + lane) * 16),
+                         xr + (col0 + 32 * q) * 4);
+            }
+          }
+        }
+        cp_async_commit();
+      }
+      if (b > 0) {
+        // ---- consume batch b-1 (issued one stage ago) ----
+        if (b < nbatches) {
+          cp_async_wait<1>();
+        } else {
+          cp_async_wait<0>();
+        }
+        const int pstage = stage ^ 1;
+        const float4* pring = ring + pstage * kAsyncBatch * kRowF4;
+        for (int j = 0; j < prev_cnt; ++j) {
+          const int rk = __shfl_sync(kFull, prev_ri, j);
+          const float wk = __shfl_sync(kFull, prev_w, j);
+          while (cur < rk) {
+            flush();
+            ++cur;
+          }
+#pragma unroll
+          for (int q = 0; q < NV; ++q) {
+            if (valid[q]) {
+              const float4 val = pring[j * kRowF4 + q * 32 + lane];
+              if constexpr (WM == kUnit) {
+                acc[q] = add4(acc[q], val);
+              } else {
+                acc[q] = fma4(wk, val, acc[q]);
+              }
+            }
+          }
+        }
+      }
+      prev_cnt = cnt;
+      prev_ri = ri;
+      prev_w = w;
+      stage ^= 1;
+    }
+    while (cur < 32 && s0 + cur < a.n) {
+      flush();
+      ++cur;
+    }
+  }
+}
+
 // Scalar kernel for feature widths that are not a multiple of 4 (or unaligned
 // pointers): one warp per row, lane l owns features l, l+32, l+64, l+96 of the
 // block's 128-feature tile; plain CSR order for every row.
@@ -546,10 +837,43 @@ int launch_vec(SpmmArgs a, cudaStream_t stream) {
     return GNN_OK;
   }
 
+  if (config().spmm_kernel.load() == 2) {
+    // asynchronous-staging kernel: one block per SM, 192 KiB of ring per block
+    const int warps = std::min(12, 12 / nv);
+    const size_t ring = static_cast<size_t>(warps) * kAsyncStages * kAsyncBatch * 32 * nv * sizeof(float4);
+    const int64_t items_a = (a.n + 31) / 32;
+    int64_t gxa = std::max<int64_t>((items_a + warps - 1) / warps,
+                                    a.long_cap > 0 ? std::min<int64_t>(a.long_cap, sm_count()) : 1);
+    gxa = std::max<int64_t>(1, std::min<int64_t>(gxa, sm_count()));
+    dim3 grid_a(static_cast<unsigned>(gxa), static_cast<unsigned>(tiles));
+    static int configured[64][4] = {};
+    int dev = 0;
+    GNN_CUDA_TRY(cudaGetDevice(&dev), "cudaGetDevice");
+#define GNN_LAUNCH_NV(NVV)                                                                                   \
+  do {                                                                                                       \
+    if (dev < 0 || dev >= 64 || !configured[dev][NVV - 1]) {                                                 \
+      GNN_CUDA_TRY(cudaFuncSetAttribute(spmm_async_kernel<WM, MEAN, HOT, NVV, IdxT>,                         \
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(ring)), \
+                   "spmm_async_kernel: shared memory opt-in");                                               \
+      if (dev >= 0 && dev < 64) configured[dev][NVV - 1] = 1;                                                \
+    }                                                                                                        \
+    spmm_async_kernel<WM, MEAN, HOT, NVV, IdxT><<<grid_a, warps * 32, ring, stream>>>(a);                    \
+  } while (0)
+    switch (nv) {
+      case 1: GNN_LAUNCH_NV(1); break;
+      case 2: GNN_LAUNCH_NV(2); break;
+      case 3: GNN_LAUNCH_NV(3); break;
+      default: GNN_LAUNCH_NV(4); break;
+    }
+#undef GNN_LAUNCH_NV
+    GNN_LAUNCH_CHECK("spmm async kernel launch");
+    return GNN_OK;
+  }
+
   // persistent packed-stream kernel: as many blocks as are resident at once
   // (2 per SM at 64 registers x 512 threads), fewer for small graphs
   const int64_t items = (a.n + 31) / 32;
-  const int64_t resident = 2LL * sm_count();
+  const int64_t resident = static_cast<int64_t>(GNN_SPMM_MIN_BLOCKS) * sm_count();
   int64_t gx = std::max<int64_t>((items + nwarps - 1) / nwarps, a.long_cap > 0 ? std::min(a.long_cap, resident) : 1);
   gx = std::max<int64_t>(1, std::min(gx, resident));
   dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(tiles));
@@ -624,6 +948,7 @@ int run_typed(const SpmmRequest& q, cudaStream_t stream) {
   // Stream degrees are summed in 32-bit over 32 rows, so the threshold is capped at 2^25.
   a.long_thr = std::min<int64_t>(resolve_long_threshold(q.n, q.nnz), int64_t(1) << 25);
   a.long_cap = std::min<int64_t>(long_capacity(q.n, q.nnz), q.nnz / (a.long_thr + 1) + 1);
+  a.long_split = static_cast<int>(config().long_row_warps.load());
   if (q.nnz <= a.long_thr) a.long_cap = 0;  // no row can be long
   // the workspace holds the work tickets (and the long-row list when needed)
   if (q.ws == nullptr || q.ws_bytes < gnn_spmm_workspace_bytes(q.n, q.nnz)) {

@@ -68,8 +68,9 @@ const char* gnn_last_error(void);     /* thread-local; "" after a success  */
 const char* gnn_status_string(int status);
 /* Tuning knobs (process-wide). Names: "spmm.long_row_threshold" (edges; 0 =
  * automatic), "spmm.long_row_warps" (4..16), "spmm.kernel" (0 = persistent
- * packed-stream kernel, the default; 1 = one warp per row; both give identical
- * results). Returns GNN_ERR_INVALID_ARGUMENT
+ * packed-stream kernel; 1 = one warp per row, the default; 2 = packed stream
+ * with cp.async staging through shared memory; all give identical results).
+ * Returns GNN_ERR_INVALID_ARGUMENT
  * for an unknown name or out-of-range value. */
 int gnn_config_set_int(const char* name, int64_t value);
 int gnn_config_get_int(const char* name, int64_t* value);

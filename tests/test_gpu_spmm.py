@@ -229,16 +229,48 @@ def test_stream_and_per_row_kernels_identical(f):
     outs = []
     old = N.config_get("spmm.kernel")
     try:
-        for kern in (0, 1):
+        for kern in (0, 1, 2):
             N.config_set("spmm.kernel", kern)
             o = torch.full((n, f), float("nan"), device=DEV)
             gcn_ops.spmm_gcn_forward_(*t, o)
             outs.append(o.cpu().numpy())
     finally:
         N.config_set("spmm.kernel", old)
-    assert _bits_equal(outs[0], outs[1])
+    assert _bits_equal(outs[0], outs[1]) and _bits_equal(outs[0], outs[2])
     exp = O.spmm(rp, ci, x, mode=O.W_GCN, dis=dis, split_warps=16, long_thr=256)
     assert _bits_equal(outs[0], exp)
+
+
+@pytest.mark.parametrize("kern", [1, 2])
+@pytest.mark.parametrize("f", [4, 128, 256])
+def test_alternative_kernels_all_modes(kern, f):
+    """Kernels 1 and 2 against the oracle for every weight/mean mode, with long rows."""
+    n = 3000
+    s, d = _graph("hub", n, seed=14)
+    rp, ci, dis = O.gcn_normalized_csr(s.numpy(), d.numpy(), n)
+    _, _, ew = O.pyg_weighted_csr(s.numpy(), d.numpy(), n)
+    x = synth.features(n, f, seed=15).numpy()
+    t = {k: torch.from_numpy(v).to(DEV) for k, v in dict(rp=rp, ci=ci, dis=dis, ew=ew, x=x).items()}
+    old = N.config_get("spmm.kernel")
+    N.config_set("spmm.kernel", kern)
+    N.config_set("spmm.long_row_threshold", 40)
+    try:
+        cases = [(lambda o: gcn_ops.spmm_gcn_forward_(t["rp"], t["ci"], t["dis"], t["x"], o),
+                  dict(mode=O.W_GCN, dis=dis)),
+                 (lambda o: pyg_gcn_ops.spmm_pyg_gcn_forward_(t["rp"], t["ci"], t["ew"], t["x"], o),
+                  dict(mode=O.W_EDGE, ew=ew)),
+                 (lambda o: agg_ops.spmm_sum_forward_(t["rp"], t["ci"], t["x"], o), dict(mode=O.W_UNIT)),
+                 (lambda o: agg_ops.spmm_mean_forward_(t["rp"], t["ci"], t["x"], o),
+                  dict(mode=O.W_UNIT, mean=O.M_DIV)),
+                 (lambda o: agg_ops.spmm_mean_forward_(t["rp"], t["ci"], t["x"], o, hmm_optimized=True),
+                  dict(mode=O.W_UNIT, mean=O.M_RCP))]
+        for run, kw in cases:
+            o = torch.full((n, f), float("nan"), device=DEV)
+            run(o)
+            exp = O.spmm(rp, ci, x, split_warps=16, long_thr=40, **kw)
+            assert _bits_equal(o.cpu().numpy(), exp), kw
+    finally:
+        N.config_set("spmm.kernel", old)
 
 
 def test_long_row_warp_counts():
