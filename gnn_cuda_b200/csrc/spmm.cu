@@ -56,17 +56,21 @@ constexpr int64_t kMinLongThreshold = 32;
 #define GNN_SPMM_U_NV1 4
 #endif
 #ifndef GNN_SPMM_U_NV2
-#define GNN_SPMM_U_NV2 2
+#define GNN_SPMM_U_NV2 4
 #endif
 #ifndef GNN_SPMM_U_NV34
 #define GNN_SPMM_U_NV34 2
 #endif
 #ifndef GNN_SPMM_MIN_BLOCKS
-#define GNN_SPMM_MIN_BLOCKS 3
+#define GNN_SPMM_MIN_BLOCKS 3  // at F <= 128 (one float4 per lane); wider rows keep 2
 #endif
 template <int NV>
 __host__ __device__ constexpr int gather_depth() {
   return NV == 1 ? GNN_SPMM_U_NV1 : (NV == 2 ? GNN_SPMM_U_NV2 : GNN_SPMM_U_NV34);
+}
+template <int NV>
+__host__ __device__ constexpr int resident_blocks() {
+  return NV == 1 ? GNN_SPMM_MIN_BLOCKS : 2;
 }
 
 enum WeightMode : int { kUnit = 0, kGcn = 1, kEdge = 2 };
@@ -111,6 +115,20 @@ __device__ __forceinline__ const float* feature_row(const SpmmArgs& a, int c) {
   return a.x + static_cast<int64_t>(c) * a.f;
 }
 
+// This lane's float4 slice of feature row c: the row base is a 32x32->64-bit
+// multiply-add off a per-lane base pointer (x + col0), one instruction.
+template <bool HOT>
+__device__ __forceinline__ const float4* gather_row(const SpmmArgs& a, int c, int64_t col0) {
+  const uint32_t row_bytes = static_cast<uint32_t>(a.f) * 4u;
+  const float* base = a.x;
+  if constexpr (HOT) {
+    if (c < a.hot_cutoff) base = a.hot;
+  }
+  const char* lane_base = reinterpret_cast<const char*>(base + col0 * 4);
+  return reinterpret_cast<const float4*>(lane_base +
+                                         static_cast<uint64_t>(static_cast<uint32_t>(c)) * row_bytes);
+}
+
 // Accumulates edges [beg, end) of one row into acc, edge by edge in CSR order.
 // All 32 lanes of the warp must call this with the same arguments. When
 // `have_first` is set, (c_first, w_first) already hold the first 32-edge chunk's
@@ -132,32 +150,45 @@ __device__ __forceinline__ void accumulate_edges(const SpmmArgs& a, IdxT beg, Id
       c = ld_stream_i32(a.col + base + lane);
       w = edge_weight<WM>(a, rs, c, static_cast<int64_t>(base) + lane);
     }
-    for (int j = 0; j < cnt; j += U) {
+    // full groups of U edges: no per-edge guards
+    int j = 0;
+    for (; j + U <= cnt; j += U) {
       float4 v[U][NV];
 #pragma unroll
       for (int k = 0; k < U; ++k) {
-        const int ck = __shfl_sync(kFull, c, j + k);
-        if (j + k < cnt) {
-          const float4* row = reinterpret_cast<const float4*>(feature_row<HOT>(a, ck));
+        const float4* row = gather_row<HOT>(a, __shfl_sync(kFull, c, j + k), col0);
 #pragma unroll
-          for (int q = 0; q < NV; ++q) {
-            if (valid[q]) v[k][q] = ldg_f4(row + col0 + 32 * q);
-          }
+        for (int q = 0; q < NV; ++q) {
+          if (valid[q]) v[k][q] = ldg_f4(row + 32 * q);
         }
       }
 #pragma unroll
       for (int k = 0; k < U; ++k) {
         const float wk = __shfl_sync(kFull, w, j + k);
-        if (j + k < cnt) {
 #pragma unroll
-          for (int q = 0; q < NV; ++q) {
-            if (valid[q]) {
-              if constexpr (WM == kUnit) {
-                acc[q] = add4(acc[q], v[k][q]);
-              } else {
-                acc[q] = fma4(wk, v[k][q], acc[q]);
-              }
+        for (int q = 0; q < NV; ++q) {
+          if (valid[q]) {
+            if constexpr (WM == kUnit) {
+              acc[q] = add4(acc[q], v[k][q]);
+            } else {
+              acc[q] = fma4(wk, v[k][q], acc[q]);
             }
+          }
+        }
+      }
+    }
+    // the remaining cnt % U edges, one at a time
+    for (; j < cnt; ++j) {
+      const float4* row = gather_row<HOT>(a, __shfl_sync(kFull, c, j), col0);
+      const float wk = __shfl_sync(kFull, w, j);
+#pragma unroll
+      for (int q = 0; q < NV; ++q) {
+        if (valid[q]) {
+          const float4 v = ldg_f4(row + 32 * q);
+          if constexpr (WM == kUnit) {
+            acc[q] = add4(acc[q], v);
+          } else {
+            acc[q] = fma4(wk, v, acc[q]);
           }
         }
       }
@@ -206,7 +237,7 @@ __global__ void plan_long_rows_kernel(const IdxT* __restrict__ row_ptr, int64_t 
 // Main vector kernel. Blocks [0, num_long_blocks) serve the long-row list;
 // the rest take kRowsPerWarp rows per warp, skipping long rows.
 template <int WM, int MEAN, bool HOT, int NV, class IdxT>
-__global__ void __launch_bounds__(kBlockThreads, GNN_SPMM_MIN_BLOCKS)
+__global__ void __launch_bounds__(kBlockThreads, resident_blocks<NV>())
     spmm_vec_kernel(SpmmArgs a, int num_long_blocks) {
   constexpr int U = gather_depth<NV>();
   extern __shared__ float4 s_part[];  // [nwarps][32 * NV] (long rows only)
@@ -267,13 +298,13 @@ __global__ void __launch_bounds__(kBlockThreads, GNN_SPMM_MIN_BLOCKS)
   // neighbour rows are being gathered, so a row does not start with a
   // row_ptr -> col_ind -> gather chain of dependent loads.
   const int64_t blk = static_cast<int64_t>(blockIdx.x) - num_long_blocks;
-  int64_t my_row = -1;
+  int my_row = -1;  // row ids fit int32 (num_nodes is limited to int32 column ids)
   IdxT my_beg = 0, my_end = 0;
   float my_rs = 1.0f;
   if (lane < kRowsPerWarp) {
     const int64_t slot = (blk * kRowsPerWarp + lane) * nwarps + warp;
     if (slot < a.n) {
-      my_row = a.sched ? a.sched[slot] : slot;
+      my_row = static_cast<int>(a.sched ? a.sched[slot] : slot);
       my_beg = rp[my_row];
       my_end = rp[my_row + 1];
       if (WM == kGcn) my_rs = __ldg(a.dis_row + my_row);
@@ -296,7 +327,7 @@ __global__ void __launch_bounds__(kBlockThreads, GNN_SPMM_MIN_BLOCKS)
   float w_next = 0.0f;
   first_chunk(0, c_next, w_next);
   for (int i = 0; i < kRowsPerWarp; ++i) {
-    const int64_t r = __shfl_sync(kFull, my_row, i);
+    const int64_t r = __shfl_sync(kFull, my_row, i);  // widened for the output offset
     if (r < 0) break;
     const IdxT beg = __shfl_sync(kFull, my_beg, i);
     const IdxT end = __shfl_sync(kFull, my_end, i);
@@ -335,7 +366,7 @@ __global__ void __launch_bounds__(kBlockThreads, GNN_SPMM_MIN_BLOCKS)
 // low-degree rows no longer leave lanes idle or serialise a row_ptr -> col ->
 // gather latency chain per row, and no warp waits for slower rows of its block.
 template <int WM, int MEAN, bool HOT, int NV, class IdxT>
-__global__ void __launch_bounds__(kBlockThreads, GNN_SPMM_MIN_BLOCKS) spmm_stream_kernel(SpmmArgs a) {
+__global__ void __launch_bounds__(kBlockThreads, resident_blocks<NV>()) spmm_stream_kernel(SpmmArgs a) {
   constexpr int U = gather_depth<NV>();
   extern __shared__ float4 s_part[];  // [nwarps][32 * NV] (long rows only)
   __shared__ uint32_t s_ticket;
@@ -870,10 +901,10 @@ int launch_vec(SpmmArgs a, cudaStream_t stream) {
     return GNN_OK;
   }
 
-  // persistent packed-stream kernel: as many blocks as are resident at once
-  // (2 per SM at 64 registers x 512 threads), fewer for small graphs
+  // persistent packed-stream kernel: as many blocks as are resident at once,
+  // fewer for small graphs
   const int64_t items = (a.n + 31) / 32;
-  const int64_t resident = static_cast<int64_t>(GNN_SPMM_MIN_BLOCKS) * sm_count();
+  const int64_t resident = static_cast<int64_t>(nv == 1 ? resident_blocks<1>() : resident_blocks<2>()) * sm_count();
   int64_t gx = std::max<int64_t>((items + nwarps - 1) / nwarps, a.long_cap > 0 ? std::min(a.long_cap, resident) : 1);
   gx = std::max<int64_t>(1, std::min(gx, resident));
   dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(tiles));
