@@ -162,16 +162,16 @@ def build_problem(seed: int, device: torch.device, scale: float):
     bs = [torch.zeros(FEAT, device=device) for _ in range(LAYERS)]
     torch.cuda.synchronize(device)
     log(f"[bench] graph n={n} nnz={ci.numel()} built in {time.time() - t0:.1f}s")
-    return dict(n=n, rp=rp, ci=ci, dis=dis, x=x, ws=ws, bs=bs)
+    return dict(n=n, nnz=int(ci.numel()), rp=rp, ci=ci, dis=dis, x=x, ws=ws, bs=bs)
 
 
 def describe(prob, world: int, gemm: str | None = None) -> dict:
     if gemm is None:
         gemm = "tcgen05-tf32" if N.lib().gnn_gemm_uses_tensor_cores(prob["n"], FEAT, FEAT) else "ffma-fp32"
     return {"workload": f"{WORKLOAD}: GCN {LAYERS} layers {FEAT}->{FEAT}->{FEAT}, ReLU between layers",
-            "nodes": prob["n"], "csr_entries": int(prob["ci"].numel()), "feat_dim": FEAT, "layers": LAYERS,
+            "nodes": prob["n"], "csr_entries": int(prob["nnz"]), "feat_dim": FEAT, "layers": LAYERS,
             "self_loops": True, "graph": "R-MAT(0.57,0.19,0.19,0.05), symmetrised, de-duplicated",
-            "parallelism": f"rows{world}" + ("" if world == 1 else "+nccl_row_exchange"),
+            "parallelism": f"rows{world}" + ("" if world == 1 else "+nccl_allgather_padded"),
             "l2": "inputs larger than L2 (X is %.2f GB), no flush" % (prob["n"] * FEAT * 4 / 1e9),
             "gemm": gemm}
 
@@ -185,14 +185,22 @@ def run_ours(args, rank: int, world: int, device: torch.device):
     n = prob["n"]
     nnz = int(prob["ci"].numel())
     rp_cpu = prob["rp"].to(torch.int64).cpu().numpy()
-    bounds = partition.nnz_balanced_bounds(rp_cpu, world)
-    r0, r1 = bounds[rank], bounds[rank + 1]
-    shard = partition.make_shard(prob["rp"], prob["ci"], r0, r1)
+    if world == 1:
+        shard = partition.make_shard(prob["rp"], prob["ci"], 0, n)
+        bufs = {"agg": torch.empty(n, FEAT, device=device), "out0": torch.empty(n, FEAT, device=device),
+                "out1": torch.empty(n, FEAT, device=device)}
+    else:
+        # padded layout: rank r's rows at [r*M, r*M + rows_r); one all_gather per layer boundary
+        layout = partition.make_padded_layout(rp_cpu, world)
+        shard = partition.make_padded_shard(prob["rp"], prob["ci"], layout, rank)
+        prob["dis"] = layout.pad_rows(prob["dis"])
+        prob["x"] = layout.pad_rows(prob["x"])
+        del prob["rp"], prob["ci"]
+        torch.cuda.empty_cache()
+        bufs = {"agg": torch.empty(shard.num_rows, FEAT, device=device),
+                "out": torch.zeros(layout.max_rows, FEAT, device=device),
+                "x_next": torch.empty(layout.padded_rows, FEAT, device=device)}
     rows = shard.num_rows
-    bufs = {"agg": torch.empty(rows, FEAT, device=device), "out0": torch.empty(rows, FEAT, device=device),
-            "out1": torch.empty(rows, FEAT, device=device)}
-    if world > 1:
-        bufs["x_next"] = torch.empty(n, FEAT, device=device)
     torch.backends.cuda.matmul.allow_tf32 = True  # the reference driver's --tf32 default
 
     def step(timers=None):
@@ -207,8 +215,8 @@ def run_ours(args, rank: int, world: int, device: torch.device):
                 agg_ops.linear_forward_(bufs["agg"], prob["ws"][li], prob["bs"][li], out, li != LAYERS - 1)
                 x = out
             return x
-        return partition.gcn_forward_partitioned(shard, prob["dis"], prob["x"], prob["ws"], prob["bs"], bounds, rank,
-                                                 bufs, timers=timers)
+        return partition.gcn_forward_allgather(shard, prob["dis"], prob["x"], prob["ws"], prob["bs"], layout, bufs,
+                                               timers=timers)
 
     for _ in range(args.warmup):
         step()

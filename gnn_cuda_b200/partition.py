@@ -109,6 +109,83 @@ def gcn_forward_partitioned(shard: RowShard, deg_inv_sqrt: torch.Tensor, x_full:
     return out
 
 
+@dataclass
+class PaddedLayout:
+    """Rank r's rows sit at [r*max_rows, r*max_rows + rows_r) of a [world*max_rows, F] matrix.
+
+    With every shard padded to max_rows, the between-layer exchange is one
+    all_gather_into_tensor straight into the next layer's input. Global row g
+    owned by rank r maps to padded id r*max_rows + (g - bounds[r]); the map is
+    increasing, so CSR column order (and therefore every sum) is unchanged.
+    """
+    bounds: list[int]
+    max_rows: int
+
+    @property
+    def world(self) -> int:
+        return len(self.bounds) - 1
+
+    @property
+    def padded_rows(self) -> int:
+        return self.world * self.max_rows
+
+    def padded_ids(self, g: torch.Tensor) -> torch.Tensor:
+        b = torch.as_tensor(self.bounds, dtype=torch.int64, device=g.device)
+        owner = torch.searchsorted(b[1:-1], g.to(torch.int64), right=True)
+        return owner * self.max_rows + (g.to(torch.int64) - b[owner])
+
+    def pad_rows(self, full: torch.Tensor) -> torch.Tensor:
+        """[N, ...] -> [world*max_rows, ...] with zero padding rows."""
+        out = torch.zeros((self.padded_rows,) + tuple(full.shape[1:]), dtype=full.dtype, device=full.device)
+        for r in range(self.world):
+            b0, b1 = self.bounds[r], self.bounds[r + 1]
+            out[r * self.max_rows:r * self.max_rows + (b1 - b0)] = full[b0:b1]
+        return out
+
+    def unpad_rows(self, padded: torch.Tensor) -> torch.Tensor:
+        return torch.cat([padded[r * self.max_rows:r * self.max_rows + (self.bounds[r + 1] - self.bounds[r])]
+                          for r in range(self.world)])
+
+
+def make_padded_layout(row_ptr: np.ndarray, world: int) -> PaddedLayout:
+    bounds = nnz_balanced_bounds(row_ptr, world)
+    return PaddedLayout(bounds, max(1, max(bounds[i + 1] - bounds[i] for i in range(world))))
+
+
+def make_padded_shard(row_ptr: torch.Tensor, col_ind: torch.Tensor, layout: PaddedLayout, rank: int) -> RowShard:
+    """Rank `rank`'s rows with column ids rewritten to padded ids; row_begin is
+    the shard's first padded row (r*max_rows)."""
+    b0, b1 = layout.bounds[rank], layout.bounds[rank + 1]
+    s = make_shard(row_ptr, col_ind, b0, b1)
+    cols = layout.padded_ids(s.col_ind).to(torch.int32)
+    base = rank * layout.max_rows
+    return RowShard(base, base + (b1 - b0), s.row_ptr, cols.contiguous())
+
+
+def gcn_forward_allgather(shard: RowShard, dis_pad: torch.Tensor, x_pad: torch.Tensor, weights: list[torch.Tensor],
+                          biases: list[torch.Tensor], layout: PaddedLayout, bufs: dict, group=None,
+                          timers: dict | None = None) -> torch.Tensor:
+    """Multi-layer GCN over a padded-layout shard; one all_gather per layer boundary.
+
+    bufs: 'agg' [rows, F], 'out' [max_rows, F] (padding rows zero), 'x_next'
+    [world*max_rows, F]. Returns this rank's [rows, F] output rows.
+    """
+    x = x_pad
+    rows = shard.num_rows
+    layers = len(weights)
+    for li in range(layers):
+        ev = _mark(timers, "spmm_begin")
+        spmm_gcn_shard(shard, dis_pad, x, bufs["agg"])
+        _mark(timers, "spmm_end", ev)
+        out = bufs["out"]
+        native_ops.linear_forward_(bufs["agg"], weights[li], biases[li], out[:rows], li != layers - 1)
+        if li == layers - 1:
+            return out[:rows]
+        dist.all_gather_into_tensor(bufs["x_next"], out, group=group)
+        x = bufs["x_next"]
+    return bufs["out"][:rows]
+
+
 def _mark(timers: dict | None, key: str, begin=None):
     """Record a CUDA event for per-kernel timing (key 'spmm_begin' / 'spmm_end')."""
     if timers is None:

@@ -47,6 +47,7 @@ def _worker(rank, world, port, q):
         N.config_set("spmm.long_row_threshold", THR)
         torch.backends.cuda.matmul.allow_tf32 = True
         rp, ci, dis, x, ws, bs = _problem(dev)
+        # broadcast exchange over unpadded row ranges
         bounds = partition.nnz_balanced_bounds(rp.cpu().numpy(), world)
         shard = partition.make_shard(rp, ci, bounds[rank], bounds[rank + 1])
         rows = shard.num_rows
@@ -55,8 +56,19 @@ def _worker(rank, world, port, q):
         out = partition.gcn_forward_partitioned(shard, dis, x, ws, bs, bounds, rank, bufs)
         full = torch.empty(N_NODES, FEAT, device=dev)
         partition.exchange_rows(out, full, bounds, rank)
+        # padded layout, one all_gather per layer boundary
+        lay = partition.make_padded_layout(rp.cpu().numpy(), world)
+        pshard = partition.make_padded_shard(rp, ci, lay, rank)
+        pbufs = {"agg": torch.empty(pshard.num_rows, FEAT, device=dev),
+                 "out": torch.zeros(lay.max_rows, FEAT, device=dev),
+                 "x_next": torch.empty(lay.padded_rows, FEAT, device=dev)}
+        pout = partition.gcn_forward_allgather(pshard, lay.pad_rows(dis), lay.pad_rows(x), ws, bs, lay, pbufs)
+        pfull = torch.zeros(lay.max_rows, FEAT, device=dev)
+        pfull[:pshard.num_rows] = pout
+        gathered = torch.empty(lay.padded_rows, FEAT, device=dev)
+        dist.all_gather_into_tensor(gathered, pfull)
         torch.cuda.synchronize(dev)
-        q.put((rank, full.cpu().numpy()))
+        q.put((rank, full.cpu().numpy(), lay.unpad_rows(gathered).cpu().numpy()))
     finally:
         dist.destroy_process_group()
 
@@ -88,9 +100,13 @@ def test_two_gpu_partitioned_gcn_matches_single_gpu():
     procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
     for p in procs:
         p.start()
-    results = dict(q.get(timeout=300) for _ in range(2))
+    results = {}
+    for _ in range(2):
+        r, bcast, padded = q.get(timeout=300)
+        results[r] = (bcast, padded)
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
     for r in range(2):
-        assert np.array_equal(results[r].view(np.uint32), single.view(np.uint32)), r
+        assert np.array_equal(results[r][0].view(np.uint32), single.view(np.uint32)), ("broadcast", r)
+        assert np.array_equal(results[r][1].view(np.uint32), single.view(np.uint32)), ("allgather", r)

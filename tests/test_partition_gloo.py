@@ -67,6 +67,71 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
+def test_padded_layout_maps():
+    rp = np.array([0, 3, 3, 10, 12, 20, 21, 30], dtype=np.int64)  # 7 rows
+    lay = partition.make_padded_layout(rp, 3)
+    assert lay.bounds[0] == 0 and lay.bounds[-1] == 7 and lay.world == 3
+    g = torch.arange(7)
+    p = lay.padded_ids(g)
+    assert torch.all(p[1:] > p[:-1])  # increasing: CSR column order survives the remap
+    x = torch.arange(7 * 2, dtype=torch.float32).view(7, 2)
+    xp = lay.pad_rows(x)
+    assert xp.shape == (lay.padded_rows, 2)
+    assert torch.equal(xp[p], x) and torch.equal(lay.unpad_rows(xp), x)
+
+
+def _worker_padded(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from oracle import oracle as O
+        from gnn_cuda_b200.GNN_cuda_common import graph_utils as G
+        n, f = 1500, 8
+        u, v = synth.rmat_undirected(n, 11000, seed=7)
+        s, d = synth.symmetrize(u, v)
+        g = G.build_gcn_normalized_csr(s, d, num_nodes=n)
+        x = synth.features(n, f, seed=8)
+        lay = partition.make_padded_layout(g.row_ptr.numpy(), world)
+        shard = partition.make_padded_shard(g.row_ptr, g.col_ind, lay, rank)
+        dis_pad = lay.pad_rows(g.deg_inv_sqrt)
+        x_pad = lay.pad_rows(x)
+        rp_local = shard.row_ptr.numpy()
+        rows = np.repeat(np.arange(shard.num_rows) + shard.row_begin, np.diff(rp_local))
+        cols = shard.col_ind.numpy()
+        ew = (dis_pad.numpy()[rows] * dis_pad.numpy()[cols]).astype(np.float32)
+        out_local = O.spmm(rp_local, cols, x_pad.numpy(), mode=O.W_EDGE, ew=ew)
+        out = torch.zeros(lay.max_rows, f)
+        out[:shard.num_rows] = torch.from_numpy(out_local)
+        gathered = torch.empty(lay.padded_rows, f)
+        dist.all_gather_into_tensor(gathered, out)
+        q.put((rank, lay.unpad_rows(gathered).numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_padded_allgather_matches_single_rank():
+    from oracle import oracle as O
+    from gnn_cuda_b200.GNN_cuda_common import graph_utils as G
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_padded, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=120) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    n, f = 1500, 8
+    u, v = synth.rmat_undirected(n, 11000, seed=7)
+    s, d = synth.symmetrize(u, v)
+    g = G.build_gcn_normalized_csr(s, d, num_nodes=n)
+    x = synth.features(n, f, seed=8)
+    ref = O.spmm(g.row_ptr.numpy(), g.col_ind.numpy(), x.numpy(), mode=O.W_GCN, dis=g.deg_inv_sqrt.numpy())
+    for r in range(2):
+        assert np.array_equal(results[r].view(np.uint32), ref.view(np.uint32))
+
+
 def test_two_rank_exchange_matches_single_rank():
     from oracle import oracle as O
     from gnn_cuda_b200.GNN_cuda_common import graph_utils as G
