@@ -64,6 +64,9 @@ def parse_args():
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU-baseline sample time")
     ap.add_argument("--scale", type=float, default=1.0, help="scale the graph down (smoke runs only)")
+    ap.add_argument("--chunks", type=int, default=4, help="row pieces per rank, exchanged as they finish (N > 1)")
+    ap.add_argument("--exchange", choices=["push", "allgather"], default="push",
+                    help="N > 1: copy-engine pushes over IPC mappings, or NCCL all_gather on a padded layout")
     return ap.parse_args()
 
 
@@ -165,13 +168,15 @@ def build_problem(seed: int, device: torch.device, scale: float):
     return dict(n=n, nnz=int(ci.numel()), rp=rp, ci=ci, dis=dis, x=x, ws=ws, bs=bs)
 
 
-def describe(prob, world: int, gemm: str | None = None) -> dict:
+def describe(prob, world: int, gemm: str | None = None, chunks: int = 1, exchange: str = "push") -> dict:
     if gemm is None:
         gemm = "tcgen05-tf32" if N.lib().gnn_gemm_uses_tensor_cores(prob["n"], FEAT, FEAT) else "ffma-fp32"
     return {"workload": f"{WORKLOAD}: GCN {LAYERS} layers {FEAT}->{FEAT}->{FEAT}, ReLU between layers",
             "nodes": prob["n"], "csr_entries": int(prob["nnz"]), "feat_dim": FEAT, "layers": LAYERS,
             "self_loops": True, "graph": "R-MAT(0.57,0.19,0.19,0.05), symmetrised, de-duplicated",
-            "parallelism": f"rows{world}" + ("" if world == 1 else "+nccl_allgather_padded"),
+            "parallelism": f"rows{world}" + ("" if world == 1 else
+                                             f"+ce_push_ipc_pieces{chunks}" if exchange == "push" else
+                                             f"+nccl_allgather_padded_pieces{chunks}"),
             "l2": "inputs larger than L2 (X is %.2f GB), no flush" % (prob["n"] * FEAT * 4 / 1e9),
             "gemm": gemm}
 
@@ -185,21 +190,30 @@ def run_ours(args, rank: int, world: int, device: torch.device):
     n = prob["n"]
     nnz = int(prob["ci"].numel())
     rp_cpu = prob["rp"].to(torch.int64).cpu().numpy()
+    exchange = None
     if world == 1:
         shard = partition.make_shard(prob["rp"], prob["ci"], 0, n)
         bufs = {"agg": torch.empty(n, FEAT, device=device), "out0": torch.empty(n, FEAT, device=device),
                 "out1": torch.empty(n, FEAT, device=device)}
+    elif args.exchange == "push":
+        # equal-nnz row ranges cut into pieces; each piece's output is pushed to the peers as it finishes
+        bounds = partition.nnz_balanced_bounds(rp_cpu, world)
+        pieces = partition.make_pieces(prob["rp"], prob["ci"], bounds[rank], bounds[rank + 1], args.chunks)
+        shard = partition.PaddedShard(rank, pieces)  # used for its row / entry counts
+        del prob["rp"], prob["ci"]
+        torch.cuda.empty_cache()
+        exchange = partition.PeerRowExchange(n, FEAT, rank, world, device)
+        bufs = {"agg": torch.empty(max(p.num_rows for p in pieces), FEAT, device=device),
+                "out": torch.empty(shard.num_rows, FEAT, device=device)}
     else:
-        # padded layout: rank r's rows at [r*M, r*M + rows_r); one all_gather per layer boundary
-        layout = partition.make_padded_layout(rp_cpu, world)
+        # padded chunk-major layout: each row piece's output is all-gathered while the next piece computes
+        layout = partition.make_padded_layout(rp_cpu, world, args.chunks)
         shard = partition.make_padded_shard(prob["rp"], prob["ci"], layout, rank)
         prob["dis"] = layout.pad_rows(prob["dis"])
         prob["x"] = layout.pad_rows(prob["x"])
         del prob["rp"], prob["ci"]
         torch.cuda.empty_cache()
-        bufs = {"agg": torch.empty(shard.num_rows, FEAT, device=device),
-                "out": torch.zeros(layout.max_rows, FEAT, device=device),
-                "x_next": torch.empty(layout.padded_rows, FEAT, device=device)}
+        bufs = partition.allgather_buffers(layout, FEAT, device)
     rows = shard.num_rows
     torch.backends.cuda.matmul.allow_tf32 = True  # the reference driver's --tf32 default
 
@@ -215,6 +229,9 @@ def run_ours(args, rank: int, world: int, device: torch.device):
                 agg_ops.linear_forward_(bufs["agg"], prob["ws"][li], prob["bs"][li], out, li != LAYERS - 1)
                 x = out
             return x
+        if args.exchange == "push":
+            return partition.gcn_forward_push(shard.pieces, prob["dis"], prob["x"], prob["ws"], prob["bs"], exchange,
+                                              bufs["agg"], bufs["out"], timers=timers)
         return partition.gcn_forward_allgather(shard, prob["dis"], prob["x"], prob["ws"], prob["bs"], layout, bufs,
                                                timers=timers)
 
@@ -239,8 +256,9 @@ def run_ours(args, rank: int, world: int, device: torch.device):
         dist.barrier()
     launches = N.lib().gnn_kernel_launches() - launches0
     ms_total = t_start.elapsed_time(t_end)
+    # SpMM time per layer on this rank (summed over its row pieces when N > 1)
     spmm_ms = [b.elapsed_time(e) for b, e in timers.get("spmm", [])]
-    spmm_ms_avg = sum(spmm_ms) / max(1, len(spmm_ms))
+    spmm_ms_avg = sum(spmm_ms) / max(1, args.steps * LAYERS)
 
     # ---- e2e through the public API with host buffers ----
     # every step copies this rank's inputs (its CSR rows, the normalisation vector,
@@ -249,7 +267,7 @@ def run_ours(args, rank: int, world: int, device: torch.device):
     if world == 1:
         dev_in = [prob["rp"], prob["ci"], prob["dis"], prob["x"]]
     else:
-        dev_in = [shard.row_ptr, shard.col_ind, prob["dis"], prob["x"]]
+        dev_in = [t for p in shard.pieces for t in (p.row_ptr, p.col_ind) if t.numel()] + [prob["dis"], prob["x"]]
     dev_in += prob["ws"] + prob["bs"]
     host_in = [t.cpu().pin_memory() for t in dev_in]
     out_host = torch.empty(rows, FEAT, pin_memory=True)
@@ -271,25 +289,29 @@ def run_ours(args, rank: int, world: int, device: torch.device):
     e2e_ms = e_start.elapsed_time(e_end)
 
     # ---- reduce over ranks ----
-    vals = torch.tensor([ms_total, e2e_ms, spmm_ms_avg, float(launches)], dtype=torch.float64, device=device)
+    # per-layer algorithmic bytes of this rank's aggregation (its rows, its CSR entries)
+    shard_bytes = spmm_layer_bytes(rows, shard.num_edges, FEAT)
+    vals = torch.tensor([ms_total, e2e_ms, spmm_ms_avg, float(launches), float(shard_bytes)], dtype=torch.float64,
+                        device=device)
+    per_rank = [vals.clone() for _ in range(world)]
     if world > 1:
-        mx = vals.clone()
-        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-        sm = vals.clone()
-        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
-        ms_total, e2e_ms, spmm_ms_avg = float(mx[0]), float(mx[1]), float(mx[2])
-        launches = int(sm[3])
+        dist.all_gather(per_rank, vals)
+    table = torch.stack(per_rank).cpu()
+    ms_total, e2e_ms = float(table[:, 0].max()), float(table[:, 1].max())
+    launches = int(table[:, 3].sum())
+    slow = int(table[:, 2].argmax())  # the rank whose aggregation took longest
+    spmm_ms_avg, shard_bytes = float(table[slow, 2]), int(table[slow, 4])
     bytes_layer = spmm_layer_bytes(n, nnz, FEAT)
     bytes_step = bytes_layer * LAYERS
     ms_step = ms_total / args.steps
     value = bytes_step / (ms_step * 1e-3) / 1e9
     e2e_value = bytes_step / ((e2e_ms / args.e2e_steps) * 1e-3) / 1e9
+    if exchange is not None:
+        exchange.close()
 
     if rank != 0:
         return None
     peak, peak_kind = measured_hbm_gbs()
-    # per-launch algorithmic bytes of the dominant kernel on one GPU (its shard)
-    shard_bytes = spmm_layer_bytes(rows, shard.num_edges, FEAT)
     achieved = shard_bytes / (spmm_ms_avg * 1e-3) / 1e9 if spmm_ms_avg > 0 else None
     traffic = profiled_traffic()
     result = {
@@ -298,12 +320,14 @@ def run_ours(args, rank: int, world: int, device: torch.device):
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
         "data": f"synthetic: seeded R-MAT graph (seed {args.seed}) with ogbn-products shape, N(0,1) features, "
                 "Glorot weights, zero bias",
-        "config": describe(prob, world),
+        "config": describe(prob, world, chunks=args.chunks, exchange=args.exchange),
         "roofline": {"bound": "hbm", "kernel": "spmm_vec_kernel (GCN aggregation)",
                      "achieved": round(achieved, 1) if achieved else None, "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4) if achieved else None, "peak_source": peak_kind,
-                     "spmm_ms_per_launch": round(spmm_ms_avg, 4), "algorithmic_bytes_per_launch": shard_bytes,
-                     "traffic": traffic},
+                     "spmm_ms_per_layer": round(spmm_ms_avg, 4), "algorithmic_bytes_per_layer": shard_bytes,
+                     "launches_per_layer": 1 if world == 1 else args.chunks,
+                     "traffic": traffic, "rank": slow,
+                     "spmm_ms_per_rank": [round(float(v), 4) for v in table[:, 2]]},
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h), "ms_per_step": round(e2e_ms / args.e2e_steps, 3),
                 "api": "gnn_cuda_b200.GNN_cuda_common.gcn_ops/agg_ops over libgnnb200.so"},

@@ -13,9 +13,16 @@ The construction here is a single sort of 64-bit (row, col) keys instead of a
 sparse-matrix library conversion. Deviation, on purpose: where the reference's
 int32 cast would silently wrap (more than 2^31-1 entries), ``index_dtype``
 int32 raises, and ``index_dtype=torch.int64`` returns an int64 ``row_ptr``.
+
+When ``src`` or ``dst`` is a CUDA tensor the CSR is built on that GPU by
+libgnnb200 (``gnn_csr_build``: a radix sort of the keys, a unique pass and a
+lower-bound search per row) and returned there; the same arrays bit for bit,
+with ``deg_inv_sqrt`` looked up in a table of the same numpy float32 values.
+CPU inputs keep the host construction, as in the reference.
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 from pathlib import Path
 
@@ -123,8 +130,87 @@ def deg_inv_sqrt_of(row_ptr: np.ndarray) -> np.ndarray:
     return np.power(np.clip(deg, np.float32(1.0), None), np.float32(-0.5)).astype(np.float32)
 
 
+def _on_device(*ts) -> torch.device | None:
+    for t in ts:
+        if isinstance(t, torch.Tensor) and t.is_cuda:
+            return t.device
+    return None
+
+
+_DEVICE_ERRORS = ("negative row index found", "negative column index found", "row index exceeds matrix dimensions",
+                  "column index exceeds matrix dimensions")
+
+
+def device_csr(rows: torch.Tensor, cols: torch.Tensor, num_nodes: int, add_self_loops: bool,
+               index_dtype: torch.dtype, device: torch.device) -> tuple[torch.Tensor, torch.Tensor, int]:
+    """(row_ptr, col_ind, max_degree) of the (row, col) pairs, built on `device` by gnn_csr_build."""
+    from .. import _native as N
+    from . import native_ops
+    if index_dtype not in (torch.int32, torch.int64):
+        raise ValueError("index_dtype must be torch.int32 or torch.int64")
+    r = torch.as_tensor(rows).to(device=device, dtype=torch.int64).contiguous()
+    c = torch.as_tensor(cols).to(device=device, dtype=torch.int64).contiguous()
+    if r.numel() != c.numel():
+        raise ValueError("row and column arrays must have the same length")
+    n, e, loops = int(num_nodes), int(r.numel()), int(bool(add_self_loops))
+    L = N.lib()
+    with torch.cuda.device(device):
+        wsb = int(L.gnn_csr_build_workspace_bytes(e, n, loops))
+        if wsb == 0:
+            raise RuntimeError(N.last_error() or "gnn_csr_build_workspace_bytes failed")
+        ws = torch.empty(wsb, dtype=torch.uint8, device=device)
+        cap = e + (n if loops else 0)
+        row_ptr = torch.empty(n + 1, dtype=index_dtype, device=device)
+        col = torch.empty(max(cap, 1), dtype=torch.int32, device=device)
+        nu, md = ctypes.c_int64(0), ctypes.c_int64(0)
+        idx = N.GNN_INDEX_INT64 if index_dtype == torch.int64 else N.GNN_INDEX_INT32
+        status = L.gnn_csr_build(r.data_ptr(), c.data_ptr(), e, n, loops, row_ptr.data_ptr(), idx, col.data_ptr(), cap,
+                                 ctypes.byref(nu), ctypes.byref(md), ws.data_ptr(), wsb, native_ops._stream(device))
+        if status != N.GNN_OK:
+            msg = N.last_error()
+            if msg in _DEVICE_ERRORS:
+                raise ValueError(msg)
+            if msg.startswith("row_ptr exceeds int32 range"):
+                raise ValueError("row_ptr exceeds int32 range; pass index_dtype=torch.int64")
+            N.check(status, "gnn_csr_build")
+    return row_ptr, col[:nu.value], int(md.value)
+
+
+def device_deg_inv_sqrt(row_ptr: torch.Tensor, num_nodes: int, max_degree: int) -> torch.Tensor:
+    """deg_inv_sqrt on row_ptr's device from a host table of numpy's float32 clip(d, 1)^-0.5."""
+    from .. import _native as N
+    from . import native_ops
+    dev = row_ptr.device
+    table = np.power(np.clip(np.arange(max(int(max_degree), 1) + 1).astype(np.float32), np.float32(1.0), None),
+                     np.float32(-0.5)).astype(np.float32)
+    t_table = torch.from_numpy(table).to(dev)
+    dis = torch.empty(int(num_nodes), dtype=torch.float32, device=dev)
+    idx = N.GNN_INDEX_INT64 if row_ptr.dtype == torch.int64 else N.GNN_INDEX_INT32
+    with torch.cuda.device(dev):
+        N.call("gnn_csr_deg_inv_sqrt", row_ptr.data_ptr(), idx, int(num_nodes), t_table.data_ptr(), table.shape[0],
+               dis.data_ptr(), native_ops._stream(dev))
+    return dis
+
+
+def device_edge_weight(row_ptr: torch.Tensor, col_ind: torch.Tensor, dis: torch.Tensor) -> torch.Tensor:
+    from .. import _native as N
+    from . import native_ops
+    dev = row_ptr.device
+    ew = torch.empty(int(col_ind.numel()), dtype=torch.float32, device=dev)
+    idx = N.GNN_INDEX_INT64 if row_ptr.dtype == torch.int64 else N.GNN_INDEX_INT32
+    with torch.cuda.device(dev):
+        N.call("gnn_csr_edge_weight", row_ptr.data_ptr(), idx, col_ind.data_ptr(), dis.data_ptr(), int(dis.numel()),
+               ew.data_ptr(), native_ops._stream(dev))
+    return ew
+
+
 def build_gcn_normalized_csr(src, dst, *, num_nodes: int, add_self_loops: bool = True,
                              index_dtype: torch.dtype = torch.int32) -> NormalizedCSR:
+    dev = _on_device(src, dst)
+    if dev is not None:
+        row_ptr, col, md = device_csr(dst, src, num_nodes, add_self_loops, index_dtype, dev)
+        return NormalizedCSR(row_ptr=row_ptr, col_ind=col, deg_inv_sqrt=device_deg_inv_sqrt(row_ptr, num_nodes, md),
+                             num_nodes=int(num_nodes), num_edges=int(col.numel()))
     r, c = _pairs(src, dst, num_nodes, add_self_loops, dst_major=True)
     row_ptr, col = csr_from_pairs(r, c, num_nodes)
     return NormalizedCSR(row_ptr=_index(row_ptr, index_dtype, "row_ptr"), col_ind=_index(col, torch.int32, "col_ind"),
@@ -134,6 +220,12 @@ def build_gcn_normalized_csr(src, dst, *, num_nodes: int, add_self_loops: bool =
 
 def build_pyg_gcn_weighted_csr(src, dst, *, num_nodes: int, add_self_loops: bool = True,
                                index_dtype: torch.dtype = torch.int32) -> WeightedCSR:
+    dev = _on_device(src, dst)
+    if dev is not None:
+        row_ptr, col, md = device_csr(dst, src, num_nodes, add_self_loops, index_dtype, dev)
+        dis = device_deg_inv_sqrt(row_ptr, num_nodes, md)
+        return WeightedCSR(row_ptr=row_ptr, col_ind=col, edge_weight=device_edge_weight(row_ptr, col, dis),
+                           num_nodes=int(num_nodes), num_edges=int(col.numel()))
     r, c = _pairs(src, dst, num_nodes, add_self_loops, dst_major=True)
     row_ptr, col = csr_from_pairs(r, c, num_nodes)
     dis = deg_inv_sqrt_of(row_ptr)
@@ -146,6 +238,11 @@ def build_pyg_gcn_weighted_csr(src, dst, *, num_nodes: int, add_self_loops: bool
 
 def build_plain_csr(src, dst, *, num_nodes: int, add_self_loops: bool = False, transpose_for_incoming: bool = True,
                     index_dtype: torch.dtype = torch.int32) -> PlainCSR:
+    dev = _on_device(src, dst)
+    if dev is not None:
+        rows, cols = (dst, src) if transpose_for_incoming else (src, dst)
+        row_ptr, col, _ = device_csr(rows, cols, num_nodes, add_self_loops, index_dtype, dev)
+        return PlainCSR(row_ptr=row_ptr, col_ind=col, num_nodes=int(num_nodes), num_edges=int(col.numel()))
     r, c = _pairs(src, dst, num_nodes, add_self_loops, dst_major=transpose_for_incoming)
     row_ptr, col = csr_from_pairs(r, c, num_nodes)
     return PlainCSR(row_ptr=_index(row_ptr, index_dtype, "row_ptr"), col_ind=_index(col, torch.int32, "col_ind"),

@@ -77,6 +77,19 @@ PROTOTYPES: dict[str, tuple[object, list[object]]] = {
     "gnn_advise_read_mostly": (_i32, [_vp, _sz, _i32, _i32]),
     "gnn_pointer_info_query": (_i32, [_vp, ctypes.POINTER(gnn_pointer_info)]),
     "gnn_device_accessible_ptr": (_i32, [_vp, ctypes.POINTER(_vp)]),
+    "gnn_csr_build_workspace_bytes": (_sz, [_i64, _i64, _i32]),
+    "gnn_csr_build": (_i32, [_vp, _vp, _i64, _i64, _i32, _vp, _i32, _vp, _i64, ctypes.POINTER(_i64),
+                             ctypes.POINTER(_i64), _vp, _sz, _vp]),
+    "gnn_csr_deg_inv_sqrt": (_i32, [_vp, _i32, _i64, _vp, _i64, _vp, _vp]),
+    "gnn_csr_edge_weight": (_i32, [_vp, _i32, _vp, _vp, _i64, _vp, _vp]),
+    "gnn_peer_alloc": (_i32, [_sz, _i32, ctypes.POINTER(_vp)]),
+    "gnn_peer_free": (_i32, [_vp, _i32]),
+    "gnn_ipc_handle_bytes": (_sz, []),
+    "gnn_ipc_get_handle": (_i32, [_vp, _vp, _sz]),
+    "gnn_ipc_open": (_i32, [_vp, _sz, _i32, ctypes.POINTER(_vp)]),
+    "gnn_ipc_close": (_i32, [_vp, _i32]),
+    "gnn_can_access_peer": (_i32, [_i32, _i32, ctypes.POINTER(_i32)]),
+    "gnn_copy_async": (_i32, [_vp, _vp, _sz, _vp]),
 }
 
 

@@ -487,11 +487,19 @@ int tc_status_read(int reset, int* status) {
 
 }  // namespace gnnb200
 
+namespace gnnb200 {
+int spmm_status_read(int reset, int* status);  // spmm.cu
+}
+
 extern "C" int gnn_device_status(int reset, int* status) {
   GNN_REQUIRE(status != nullptr, GNN_ERR_NULL_POINTER, "status must not be NULL");
-  const int rc = gnnb200::tc_status_read(reset, status);
-  if (rc == GNN_OK) gnnb200::clear_error();
-  return rc;
+  int tc = 0, sp = 0;
+  int rc = gnnb200::tc_status_read(reset, &tc);
+  if (rc == GNN_OK) rc = gnnb200::spmm_status_read(reset, &sp);
+  if (rc != GNN_OK) return rc;
+  *status = tc != 0 ? tc : sp;
+  gnnb200::clear_error();
+  return GNN_OK;
 }
 
 extern "C" int gnn_gemm_uses_tensor_cores(int64_t m, int64_t k, int64_t n) {

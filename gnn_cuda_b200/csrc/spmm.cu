@@ -21,7 +21,12 @@
 //     kernel lists them in the caller's workspace; the first CTAs of the main
 //     grid pull them from that list with an atomic ticket and split each one
 //     into contiguous per-warp edge ranges. The warp partials are added in warp
-//     order through shared memory: deterministic, no float atomics.
+//     order through shared memory: deterministic, no float atomics. A row
+//     longer than one CTA's segment (warps x 512 entries) is cut into
+//     segments that separate CTAs take in ticket order; segment k adds its
+//     partial to the row after segment k-1 has stored its own (a bounded wait
+//     on a per-row counter), so a 10^5-entry hub costs ~512 dependent gathers
+//     per warp instead of deg/16, and the sum order stays fixed.
 //   * Feature widths that are not a multiple of 4 (or unaligned bases) use a
 //     scalar warp-per-row kernel in plain CSR order.
 #include <cuda_runtime.h>
@@ -44,9 +49,21 @@ constexpr int kRowsPerWarp = GNN_SPMM_ROWS_PER_WARP;  // rows a warp takes per b
 constexpr int kTileF4 = 128;             // float4 columns per feature tile (512 floats)
 constexpr int kMaxTiles = 30;            // per-tile tickets live in the workspace header
 constexpr size_t kWsHeader = 256;        // uint32 counters, see below
-constexpr int kLongTicket = 2;           // [0] long-row count, [2+t] long-row ticket of tile t
-constexpr int kItemTicket = 32;          // [32+t] work-item ticket of tile t
+// Workspace header (uint32 words): [0] single-segment long rows listed,
+// [1] segments of multi-segment rows listed, [2] long-work ticket (shared by
+// all feature tiles), [32+t] work-item ticket of tile t.
+constexpr int kHdrLongCount = 0;
+constexpr int kHdrSegCount = 1;
+constexpr int kHdrLongTicket = 2;
+constexpr int kItemTicket = 32;
 constexpr int64_t kMinLongThreshold = 32;
+// A long row is summed by one CTA in segments of long_split * kSegEdgesPerWarp
+// entries: each warp of the CTA takes at most this many entries of a segment.
+constexpr int64_t kSegEdgesPerWarp = 512;
+constexpr int64_t kMinSegLen = 4 * kSegEdgesPerWarp;  // spmm.long_row_warps >= 4
+constexpr int kChainTimeout = 16;  // status code: a segment gave up waiting for its predecessor
+constexpr int kPlanOverflow = 17;  // status code: long-row lists overflowed (num_edges too small)
+constexpr uint32_t kSegTag = 0x80000000u;
 
 // Neighbour rows a warp gathers per round (rows in flight per warp) and the
 // number of 512-thread blocks kept resident per SM. Measured on B200: a few
@@ -91,10 +108,21 @@ struct SpmmArgs {
   int64_t f;
   int64_t long_thr;
   uint32_t* counters;
-  uint32_t* long_list;
+  uint32_t* long_list;      // single-segment long rows
   int64_t long_cap;
-  int long_split;          // chunks per long row (spmm.long_row_warps)
+  // Segments of multi-segment rows, one uint2 each: .x = row; .y = k | kSegTag
+  // for segment k > 0, and for segment 0 (.y tag bit clear) the row's chain
+  // counter: the number of (segment, tile) units of the row already stored.
+  uint2* seg_items;
+  int64_t seg_cap;
+  int64_t seg_len;          // entries per segment (long_split * kSegEdgesPerWarp)
+  int tiles;                // feature tiles (grid.y)
+  int long_split;           // warps per segment (spmm.long_row_warps)
 };
+
+// Set by a segment whose bounded wait for its predecessor ran out (the row is
+// then wrong); read and cleared through gnn_device_status.
+__device__ int g_spmm_status = 0;
 
 template <int WM>
 __device__ __forceinline__ float edge_weight(const SpmmArgs& a, float rs, int c, int64_t e) {
@@ -218,19 +246,152 @@ __device__ __forceinline__ float4 finish(float4 acc, int64_t deg) {
   return acc;
 }
 
-// Lists the rows whose degree exceeds the long-row threshold.
+// Lists the rows whose degree exceeds the long-row threshold: rows that fit
+// one segment go to `list`; a longer row reserves ceil(deg / seg_len)
+// consecutive segment slots and writes (row, 0) into the first (its chain
+// counter starts at 0) and (row, k | kSegTag) into the others.
 template <class IdxT>
 __global__ void plan_long_rows_kernel(const IdxT* __restrict__ row_ptr, int64_t n, int64_t thr,
-                                      uint32_t* __restrict__ counters,
-                                      uint32_t* __restrict__ list, int64_t cap) {
+                                      int64_t seg_len, uint32_t* __restrict__ counters,
+                                      uint32_t* __restrict__ list, int64_t cap,
+                                      uint2* __restrict__ seg_items, int64_t seg_cap) {
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t r = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; r < n;
        r += stride) {
     const int64_t deg = static_cast<int64_t>(row_ptr[r + 1]) - static_cast<int64_t>(row_ptr[r]);
-    if (deg > thr) {
-      const uint32_t i = atomicAdd(&counters[0], 1u);
+    if (deg <= thr) continue;
+    if (deg <= seg_len) {
+      const uint32_t i = atomicAdd(&counters[kHdrLongCount], 1u);
       if (i < cap) list[i] = static_cast<uint32_t>(r);
+    } else {
+      const int64_t nk = (deg + seg_len - 1) / seg_len;
+      const uint32_t base = atomicAdd(&counters[kHdrSegCount], static_cast<uint32_t>(nk));
+      if (static_cast<int64_t>(base) + nk <= seg_cap) {
+        for (int64_t k = 0; k < nk; ++k) {
+          const uint32_t tag = k == 0 ? 0u : (static_cast<uint32_t>(k) | kSegTag);
+          seg_items[base + k] = make_uint2(static_cast<uint32_t>(r), tag);
+        }
+      }
     }
+  }
+}
+
+// Thread-level bounded wait until *p >= target (acquire). ~2 s at most.
+__device__ __forceinline__ bool wait_at_least(const uint32_t* p, uint32_t target) {
+  for (uint32_t it = 0; it < (1u << 24); ++it) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    if (v >= target) return true;
+    __nanosleep(128);
+  }
+  return false;
+}
+
+// Long-row phase shared by every vector kernel. Work units, taken with one
+// atomic ticket in this order: the segments of multi-segment rows (segment
+// major, feature tile minor), then the single-segment long rows. A unit is
+// summed by the whole CTA: its segment is cut into long_split contiguous
+// chunks (warp w takes chunks w, w + nwarps, ...), each summed edge by edge in
+// CSR order, and the chunk partials are added in chunk order through shared
+// memory. Segment k > 0 then waits until every tile of segments 0..k-1 has
+// stored, and adds its partial to the stored prefix: row = ((s0 + s1) + s2)...
+// Tickets are handed out in unit order, so a waiting segment's predecessors
+// were taken earlier by CTAs that are running; the wait always ends.
+// Out of line by default: the long-row phase then gets its own register
+// allocation and does not raise the pressure (and spills) of the per-row path.
+#ifndef GNN_SPMM_LONG_NOINLINE
+#define GNN_SPMM_LONG_NOINLINE 1
+#endif
+#if GNN_SPMM_LONG_NOINLINE
+#define GNN_LONG_PHASE_INLINE __noinline__
+#else
+#define GNN_LONG_PHASE_INLINE __forceinline__
+#endif
+template <int WM, int MEAN, bool HOT, int NV, class IdxT>
+__device__ GNN_LONG_PHASE_INLINE void long_rows_phase(const SpmmArgs& a, float4* s_part, uint32_t* s_ticket) {
+  constexpr int U = gather_depth<NV>();
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int nwarps = blockDim.x >> 5;
+  const int split = a.long_split;
+  const int64_t f4 = a.f >> 2;
+  const IdxT* __restrict__ rp = static_cast<const IdxT*>(a.row_ptr);
+  const uint32_t tiles = static_cast<uint32_t>(a.tiles);
+  uint32_t nseg = __ldcg(&a.counters[kHdrSegCount]);
+  uint32_t nlong = __ldcg(&a.counters[kHdrLongCount]);
+  if (nseg > a.seg_cap || nlong > a.long_cap) {
+    // only possible when num_edges understates the entries row_ptr spans:
+    // the lists are incomplete, so their rows are not computed and this is flagged
+    if (threadIdx.x == 0) atomicCAS(&g_spmm_status, 0, kPlanOverflow);
+    nseg = 0;
+    nlong = 0;
+  }
+  const uint64_t total = static_cast<uint64_t>(nseg + nlong) * tiles;
+  while (true) {
+    if (threadIdx.x == 0) *s_ticket = atomicAdd(&a.counters[kHdrLongTicket], 1u);
+    __syncthreads();
+    const uint32_t t = *s_ticket;
+    __syncthreads();
+    if (t >= total) break;
+    const uint32_t unit = t / tiles;
+    const int tile = static_cast<int>(t - unit * tiles);
+    int64_t r, k = 0, nk = 1;
+    uint32_t head = 0;
+    if (unit < nseg) {
+      const uint2 it = __ldcg(a.seg_items + unit);  // a head's .y may already count stored units
+      r = it.x;
+      k = (it.y & kSegTag) ? (it.y & ~kSegTag) : 0;
+      head = unit - static_cast<uint32_t>(k);
+    } else {
+      r = a.long_list[unit - nseg];
+    }
+    const IdxT beg = rp[r];
+    const IdxT end = rp[r + 1];
+    const int64_t deg = static_cast<int64_t>(end - beg);
+    if (unit < nseg) nk = (deg + a.seg_len - 1) / a.seg_len;
+    const int64_t sb = static_cast<int64_t>(beg) + k * a.seg_len;
+    const int64_t se = min(sb + a.seg_len, static_cast<int64_t>(end));
+    const int64_t chunk = (se - sb + split - 1) / split;
+    const int64_t col0 = static_cast<int64_t>(tile) * kTileF4 + lane;
+    bool valid[NV];
+#pragma unroll
+    for (int q = 0; q < NV; ++q) valid[q] = (col0 + 32 * q) < f4;
+    const float rs = (WM == kGcn) ? __ldg(a.dis_row + r) : 1.0f;
+    for (int c = warp; c < split; c += nwarps) {
+      const int64_t wb = min(sb + c * chunk, se);
+      const int64_t we = min(wb + chunk, se);
+      float4 acc[NV];
+#pragma unroll
+      for (int q = 0; q < NV; ++q) acc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+      accumulate_edges<WM, HOT, NV, U, IdxT>(a, static_cast<IdxT>(wb), static_cast<IdxT>(we), rs, lane, col0,
+                                             valid, acc);
+#pragma unroll
+      for (int q = 0; q < NV; ++q) s_part[c * 32 * NV + q * 32 + lane] = acc[q];
+    }
+    __syncthreads();
+    if (k > 0) {
+      if (threadIdx.x == 0 && !wait_at_least(&a.seg_items[head].y, static_cast<uint32_t>(k) * tiles)) {
+        atomicCAS(&g_spmm_status, 0, kChainTimeout);
+      }
+      __syncthreads();
+    }
+    float4* orow = reinterpret_cast<float4*>(a.out + r * a.f);
+    for (int j = threadIdx.x; j < 32 * NV; j += blockDim.x) {
+      const int64_t cj = static_cast<int64_t>(tile) * kTileF4 + j;
+      if (cj < f4) {
+        float4 s = s_part[j];
+        for (int w = 1; w < split; ++w) s = add4(s, s_part[w * 32 * NV + j]);
+        if (k > 0) s = add4(__ldcg(orow + cj), s);
+        if (k == nk - 1) s = finish<MEAN>(s, deg);
+        orow[cj] = s;
+      }
+    }
+    if (k < nk - 1) {
+      __threadfence();
+      __syncthreads();
+      if (threadIdx.x == 0) atomicAdd(&a.seg_items[head].y, 1u);
+    }
+    __syncthreads();
   }
 }
 
@@ -255,40 +416,8 @@ __global__ void __launch_bounds__(kBlockThreads, resident_blocks<NV>())
   const IdxT* __restrict__ rp = static_cast<const IdxT*>(a.row_ptr);
 
   if (static_cast<int>(blockIdx.x) < num_long_blocks) {
-    // ---- long rows: one row per CTA iteration, split across all warps ----
-    const uint32_t count = min(__ldcg(&a.counters[0]), static_cast<uint32_t>(a.long_cap));
-    while (true) {
-      if (threadIdx.x == 0) s_ticket = atomicAdd(&a.counters[2 + tile], 1u);
-      __syncthreads();
-      const uint32_t t = s_ticket;
-      if (t >= count) break;
-      const int64_t r = a.long_list[t];
-      const IdxT beg = rp[r];
-      const IdxT end = rp[r + 1];
-      const int64_t deg = static_cast<int64_t>(end - beg);
-      const int64_t chunk = (deg + nwarps - 1) / nwarps;
-      const IdxT wb = static_cast<IdxT>(min(static_cast<int64_t>(beg) + warp * chunk, static_cast<int64_t>(end)));
-      const IdxT we = static_cast<IdxT>(min(static_cast<int64_t>(wb) + chunk, static_cast<int64_t>(end)));
-        const float rs = (WM == kGcn) ? __ldg(a.dis_row + r) : 1.0f;
-      float4 acc[NV];
-#pragma unroll
-      for (int q = 0; q < NV; ++q) acc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
-      accumulate_edges<WM, HOT, NV, U, IdxT>(a, wb, we, rs, lane, col0, valid, acc);
-#pragma unroll
-      for (int q = 0; q < NV; ++q) s_part[warp * 32 * NV + q * 32 + lane] = acc[q];
-      __syncthreads();
-      // fixed-order reduction over warps: ((p0 + p1) + p2) + ...
-      for (int j = threadIdx.x; j < 32 * NV; j += blockDim.x) {
-        const int64_t cj = static_cast<int64_t>(tile) * kTileF4 + j;  // float4 column
-        if (cj < f4) {
-          float4 s = s_part[j];
-          for (int w = 1; w < nwarps; ++w) s = add4(s, s_part[w * 32 * NV + j]);
-          s = finish<MEAN>(s, deg);
-          reinterpret_cast<float4*>(a.out + r * a.f)[cj] = s;
-        }
-      }
-      __syncthreads();
-    }
+    // ---- long rows and their segments, split across all warps ----
+    long_rows_phase<WM, MEAN, HOT, NV, IdxT>(a, s_part, &s_ticket);
     return;
   }
 
@@ -372,8 +501,6 @@ __global__ void __launch_bounds__(kBlockThreads, resident_blocks<NV>()) spmm_str
   __shared__ uint32_t s_ticket;
 
   const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-  const int nwarps = blockDim.x >> 5;
   const int tile = blockIdx.y;
   const int64_t f4 = a.f >> 2;
   const int64_t col0 = static_cast<int64_t>(tile) * kTileF4 + lane;
@@ -383,41 +510,7 @@ __global__ void __launch_bounds__(kBlockThreads, resident_blocks<NV>()) spmm_str
   const IdxT* __restrict__ rp = static_cast<const IdxT*>(a.row_ptr);
 
   // ---------------- phase 1: long rows ----------------
-  if (a.long_cap > 0) {
-    const uint32_t count = min(__ldcg(&a.counters[0]), static_cast<uint32_t>(a.long_cap));
-    while (true) {
-      if (threadIdx.x == 0) s_ticket = atomicAdd(&a.counters[kLongTicket + tile], 1u);
-      __syncthreads();
-      const uint32_t t = s_ticket;
-      __syncthreads();
-      if (t >= count) break;
-      const int64_t r = a.long_list[t];
-      const IdxT beg = rp[r];
-      const IdxT end = rp[r + 1];
-      const int64_t deg = static_cast<int64_t>(end - beg);
-      const int64_t chunk = (deg + nwarps - 1) / nwarps;
-      const IdxT wb = static_cast<IdxT>(min(static_cast<int64_t>(beg) + warp * chunk, static_cast<int64_t>(end)));
-      const IdxT we = static_cast<IdxT>(min(static_cast<int64_t>(wb) + chunk, static_cast<int64_t>(end)));
-      const float rs = (WM == kGcn) ? __ldg(a.dis_row + r) : 1.0f;
-      float4 acc[NV];
-#pragma unroll
-      for (int q = 0; q < NV; ++q) acc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
-      accumulate_edges<WM, HOT, NV, U, IdxT>(a, wb, we, rs, lane, col0, valid, acc);
-#pragma unroll
-      for (int q = 0; q < NV; ++q) s_part[warp * 32 * NV + q * 32 + lane] = acc[q];
-      __syncthreads();
-      for (int j = threadIdx.x; j < 32 * NV; j += blockDim.x) {
-        const int64_t cj = static_cast<int64_t>(tile) * kTileF4 + j;
-        if (cj < f4) {
-          float4 s = s_part[j];
-          for (int w = 1; w < nwarps; ++w) s = add4(s, s_part[w * 32 * NV + j]);
-          s = finish<MEAN>(s, deg);
-          reinterpret_cast<float4*>(a.out + r * a.f)[cj] = s;
-        }
-      }
-      __syncthreads();
-    }
-  }
+  if (a.long_cap > 0) long_rows_phase<WM, MEAN, HOT, NV, IdxT>(a, s_part, &s_ticket);
 
   // ---------------- phase 2: packed streams of short rows ----------------
   const int64_t items = (a.n + 31) >> 5;
@@ -573,7 +666,6 @@ __global__ void __launch_bounds__(384, 1) spmm_async_kernel(SpmmArgs a) {
 
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  const int nwarps = blockDim.x >> 5;
   const int tile = blockIdx.y;
   const int64_t f4 = a.f >> 2;
   const int64_t col0 = static_cast<int64_t>(tile) * kTileF4 + lane;
@@ -585,49 +677,10 @@ __global__ void __launch_bounds__(384, 1) spmm_async_kernel(SpmmArgs a) {
   const uint32_t ring_addr = static_cast<uint32_t>(__cvta_generic_to_shared(ring));
 
   // ---------------- phase 1: long rows (register gathers) ----------------
-  // A long row is cut into a.long_split contiguous chunks (the same cut as the
-  // other kernels, whatever this block's warp count); warp w sums chunks
-  // w, w + nwarps, ... into their own shared-memory slots, which are then added
-  // in chunk order.
-  if (a.long_cap > 0) {
-    constexpr int U = gather_depth<NV>();
-    const int split = a.long_split;
-    const uint32_t count = min(__ldcg(&a.counters[0]), static_cast<uint32_t>(a.long_cap));
-    while (true) {
-      if (threadIdx.x == 0) s_ticket = atomicAdd(&a.counters[kLongTicket + tile], 1u);
-      __syncthreads();
-      const uint32_t t = s_ticket;
-      __syncthreads();
-      if (t >= count) break;
-      const int64_t r = a.long_list[t];
-      const IdxT beg = rp[r];
-      const IdxT end = rp[r + 1];
-      const int64_t deg = static_cast<int64_t>(end - beg);
-      const int64_t chunk = (deg + split - 1) / split;
-      const float rs = (WM == kGcn) ? __ldg(a.dis_row + r) : 1.0f;
-      for (int cidx = warp; cidx < split; cidx += nwarps) {
-        const IdxT wb = static_cast<IdxT>(min(static_cast<int64_t>(beg) + cidx * chunk, static_cast<int64_t>(end)));
-        const IdxT we = static_cast<IdxT>(min(static_cast<int64_t>(wb) + chunk, static_cast<int64_t>(end)));
-        float4 acc[NV];
-#pragma unroll
-        for (int q = 0; q < NV; ++q) acc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
-        accumulate_edges<WM, HOT, NV, U, IdxT>(a, wb, we, rs, lane, col0, valid, acc);
-#pragma unroll
-        for (int q = 0; q < NV; ++q) s_dyn[cidx * 32 * NV + q * 32 + lane] = acc[q];
-      }
-      __syncthreads();
-      for (int j = threadIdx.x; j < 32 * NV; j += blockDim.x) {
-        const int64_t cj = static_cast<int64_t>(tile) * kTileF4 + j;
-        if (cj < f4) {
-          float4 s = s_dyn[j];
-          for (int w = 1; w < split; ++w) s = add4(s, s_dyn[w * 32 * NV + j]);
-          s = finish<MEAN>(s, deg);
-          reinterpret_cast<float4*>(a.out + r * a.f)[cj] = s;
-        }
-      }
-      __syncthreads();
-    }
-  }
+  // The same segments and chunk cut as the other kernels, whatever this
+  // block's warp count: warp w sums chunks w, w + nwarps, ... into their own
+  // shared-memory slots (the ring), which are then added in chunk order.
+  if (a.long_cap > 0) long_rows_phase<WM, MEAN, HOT, NV, IdxT>(a, s_dyn, &s_ticket);
 
   // ---------------- phase 2: packed streams with cp.async staging ----------------
   const int64_t items = (a.n + 31) >> 5;
@@ -822,6 +875,27 @@ int64_t long_capacity(int64_t n, int64_t nnz) {
   return std::max<int64_t>(0, std::min<int64_t>(n, nnz / (kMinLongThreshold + 1) + 1));
 }
 
+// Segments of multi-segment rows: a row longer than one segment (> seg_len >=
+// kMinSegLen entries) has ceil(deg / seg_len) < 2 deg / seg_len of them.
+int64_t segment_capacity(int64_t nnz) { return nnz > kMinSegLen ? 2 * (nnz / kMinSegLen) + 1 : 0; }
+
+size_t align256(size_t b) { return (b + 255) & ~static_cast<size_t>(255); }
+
+// Workspace layout: header | long_list u32[cap] | seg_items uint2[seg_cap].
+struct WsLayout {
+  size_t list_off, seg_off, total;
+  int64_t cap, seg_cap;
+};
+WsLayout ws_layout(int64_t n, int64_t nnz) {
+  WsLayout w{};
+  w.cap = (n > 0 && nnz >= 0) ? long_capacity(n, nnz) : 0;
+  w.seg_cap = (n > 0 && nnz >= 0) ? segment_capacity(nnz) : 0;
+  w.list_off = kWsHeader;
+  w.seg_off = w.list_off + align256(static_cast<size_t>(w.cap) * sizeof(uint32_t));
+  w.total = w.seg_off + align256(static_cast<size_t>(w.seg_cap) * sizeof(uint2));
+  return w;
+}
+
 int64_t resolve_long_threshold(int64_t n, int64_t nnz) {
   int64_t thr = config().long_row_threshold.load();
   if (thr <= 0) {
@@ -851,7 +925,9 @@ int launch_vec(SpmmArgs a, cudaStream_t stream) {
   if (config().spmm_kernel.load() == 1) {
     // per-row kernel: one warp per row, blocks of consecutive rows
     int num_long_blocks = 0;
-    if (a.long_cap > 0) num_long_blocks = static_cast<int>(std::min<int64_t>(a.long_cap, 2 * sm_count()));
+    if (a.long_cap > 0) {
+      num_long_blocks = static_cast<int>(std::min<int64_t>(a.long_cap + a.seg_cap, 2 * sm_count()));
+    }
     const int64_t gx = normal_blocks + num_long_blocks;
     if (gx > 0x7fffffffLL) return fail(GNN_ERR_UNSUPPORTED, "spmm: too many rows for one launch");
     dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(tiles));
@@ -980,20 +1056,27 @@ int run_typed(const SpmmRequest& q, cudaStream_t stream) {
   a.long_thr = std::min<int64_t>(resolve_long_threshold(q.n, q.nnz), int64_t(1) << 25);
   a.long_cap = std::min<int64_t>(long_capacity(q.n, q.nnz), q.nnz / (a.long_thr + 1) + 1);
   a.long_split = static_cast<int>(config().long_row_warps.load());
+  a.seg_len = static_cast<int64_t>(a.long_split) * kSegEdgesPerWarp;
+  a.tiles = static_cast<int>(tiles);
   if (q.nnz <= a.long_thr) a.long_cap = 0;  // no row can be long
-  // the workspace holds the work tickets (and the long-row list when needed)
-  if (q.ws == nullptr || q.ws_bytes < gnn_spmm_workspace_bytes(q.n, q.nnz)) {
+  // the workspace holds the work tickets (and the long-row lists when needed)
+  const WsLayout lay = ws_layout(q.n, q.nnz);
+  if (q.ws == nullptr || q.ws_bytes < lay.total) {
     return fail(GNN_ERR_WORKSPACE, "spmm: workspace missing or smaller than gnn_spmm_workspace_bytes()");
   }
-  a.counters = static_cast<uint32_t*>(q.ws);
-  a.long_list = reinterpret_cast<uint32_t*>(static_cast<char*>(q.ws) + kWsHeader);
+  char* ws = static_cast<char*>(q.ws);
+  a.counters = reinterpret_cast<uint32_t*>(ws);
+  a.long_list = reinterpret_cast<uint32_t*>(ws + lay.list_off);
+  a.seg_items = reinterpret_cast<uint2*>(ws + lay.seg_off);
+  a.seg_cap = a.long_cap > 0 ? lay.seg_cap : 0;
   GNN_CUDA_TRY(cudaMemsetAsync(q.ws, 0, kWsHeader, stream), "spmm: workspace reset");
   if (a.long_cap > 0) {
     const int threads = 256;
     const int64_t want = (q.n + threads - 1) / threads;
     const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, 8LL * sm_count())));
     plan_long_rows_kernel<IdxT><<<blocks, threads, 0, stream>>>(
-        static_cast<const IdxT*>(q.row_ptr), q.n, a.long_thr, a.counters, a.long_list, a.long_cap);
+        static_cast<const IdxT*>(q.row_ptr), q.n, a.long_thr, a.seg_len, a.counters, a.long_list, a.long_cap,
+        a.seg_items, a.seg_cap);
     GNN_LAUNCH_CHECK("spmm plan kernel launch");
   } else {
     a.long_thr = INT64_MAX;
@@ -1072,10 +1155,19 @@ using namespace gnnb200;
 
 extern "C" size_t gnn_spmm_workspace_bytes(int64_t num_nodes, int64_t num_edges) {
   if (num_nodes <= 0 || num_edges < 0) return kWsHeader;
-  const int64_t cap = long_capacity(num_nodes, num_edges);
-  const size_t list = (static_cast<size_t>(cap) * sizeof(uint32_t) + 255) & ~static_cast<size_t>(255);
-  return kWsHeader + list;
+  return ws_layout(num_nodes, num_edges).total;
 }
+
+namespace gnnb200 {
+int spmm_status_read(int reset, int* status) {
+  GNN_CUDA_TRY(cudaMemcpyFromSymbol(status, g_spmm_status, sizeof(int)), "read spmm status word");
+  if (reset) {
+    const int zero = 0;
+    GNN_CUDA_TRY(cudaMemcpyToSymbol(g_spmm_status, &zero, sizeof(int)), "reset spmm status word");
+  }
+  return GNN_OK;
+}
+}  // namespace gnnb200
 
 static SpmmRequest make_req(const void* rp, int rpt, const int32_t* col, const float* dis,
                             const float* ew, const float* x, float* out, int64_t n, int64_t nnz,

@@ -5,13 +5,21 @@ communication inside a layer. Each rank owns a contiguous row range chosen so
 every rank holds about the same number of CSR entries (power-law graphs make
 equal-row splits badly unbalanced), keeps the full feature matrix, and after
 every layer except the last the ranks exchange their output rows so everyone
-again holds the full [N, F] input of the next layer. Ranges are unequal, so the
-exchange is one broadcast per owner rank into its slice of the full matrix
-(every slice is a contiguous row block, so no repacking is needed).
-Nothing here is model-specific; the GCN forward below is the benchmarked path.
+again holds the full [N, F] input of the next layer.
+
+Three exchanges are provided, all bit-identical to the one-GPU forward.
+`gcn_forward_push` (the benchmarked path) cuts each rank's rows into pieces,
+writes each piece's output straight into the rank's slice of the next layer's
+input and pushes it to every peer's copy with copy-engine transfers over
+CUDA IPC mappings while the next piece is computed; one small NCCL all_reduce
+per layer boundary serves as the barrier. `gcn_forward_allgather` renumbers
+rows into a padded chunk-major layout and exchanges each piece with an
+asynchronous NCCL all_gather. `gcn_forward_partitioned` keeps global row ids
+and broadcasts each owner's row range.
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 
 import numpy as np
@@ -111,83 +119,313 @@ def gcn_forward_partitioned(shard: RowShard, deg_inv_sqrt: torch.Tensor, x_full:
 
 @dataclass
 class PaddedLayout:
-    """Rank r's rows sit at [r*max_rows, r*max_rows + rows_r) of a [world*max_rows, F] matrix.
+    """Chunk-major padded row layout for an all-gather exchange that can be pipelined.
 
-    With every shard padded to max_rows, the between-layer exchange is one
-    all_gather_into_tensor straight into the next layer's input. Global row g
-    owned by rank r maps to padded id r*max_rows + (g - bounds[r]); the map is
-    increasing, so CSR column order (and therefore every sum) is unchanged.
+    Every rank's local rows are cut into `chunks` pieces of `chunk_rows` (Mc)
+    rows; local row i of rank r lives at padded id
+
+        (i // Mc) * world * Mc  +  r * Mc  +  (i % Mc)
+
+    so piece c of every rank forms the contiguous block [c*world*Mc,
+    (c+1)*world*Mc) of the padded [chunks*world*Mc, F] matrix, and exchanging
+    piece c is one all_gather_into_tensor straight into the next layer's input
+    while piece c+1 is still being computed. Padding rows are never referenced
+    by any column id. The remap only rewrites column values; the CSR entry
+    order, and therefore every floating-point sum, is unchanged. With
+    chunks == 1 this is the plain layout r*Mc + i.
     """
     bounds: list[int]
-    max_rows: int
+    chunk_rows: int
+    chunks: int = 1
 
     @property
     def world(self) -> int:
         return len(self.bounds) - 1
 
     @property
+    def local_rows(self) -> int:
+        """Rows of one rank's padded output buffer (chunks * Mc)."""
+        return self.chunks * self.chunk_rows
+
+    @property
     def padded_rows(self) -> int:
-        return self.world * self.max_rows
+        return self.chunks * self.world * self.chunk_rows
+
+    def rows_of(self, rank: int) -> int:
+        return self.bounds[rank + 1] - self.bounds[rank]
+
+    def piece_range(self, rank: int, c: int) -> tuple[int, int]:
+        """Local row range [lo, hi) of piece c on `rank` (possibly empty)."""
+        lo = min(c * self.chunk_rows, self.rows_of(rank))
+        return lo, min((c + 1) * self.chunk_rows, self.rows_of(rank))
 
     def padded_ids(self, g: torch.Tensor) -> torch.Tensor:
         b = torch.as_tensor(self.bounds, dtype=torch.int64, device=g.device)
-        owner = torch.searchsorted(b[1:-1], g.to(torch.int64), right=True)
-        return owner * self.max_rows + (g.to(torch.int64) - b[owner])
+        g = g.to(torch.int64)
+        owner = torch.searchsorted(b[1:-1], g, right=True)
+        i = g - b[owner]
+        mc = self.chunk_rows
+        return (i // mc) * (self.world * mc) + owner * mc + (i % mc)
 
     def pad_rows(self, full: torch.Tensor) -> torch.Tensor:
-        """[N, ...] -> [world*max_rows, ...] with zero padding rows."""
+        """[N, ...] -> [padded_rows, ...] with zero padding rows."""
         out = torch.zeros((self.padded_rows,) + tuple(full.shape[1:]), dtype=full.dtype, device=full.device)
-        for r in range(self.world):
-            b0, b1 = self.bounds[r], self.bounds[r + 1]
-            out[r * self.max_rows:r * self.max_rows + (b1 - b0)] = full[b0:b1]
+        out[self.padded_ids(torch.arange(full.shape[0], device=full.device))] = full
         return out
 
     def unpad_rows(self, padded: torch.Tensor) -> torch.Tensor:
-        return torch.cat([padded[r * self.max_rows:r * self.max_rows + (self.bounds[r + 1] - self.bounds[r])]
-                          for r in range(self.world)])
+        return padded[self.padded_ids(torch.arange(self.bounds[-1], device=padded.device))]
 
 
-def make_padded_layout(row_ptr: np.ndarray, world: int) -> PaddedLayout:
+def make_padded_layout(row_ptr: np.ndarray, world: int, chunks: int = 1) -> PaddedLayout:
     bounds = nnz_balanced_bounds(row_ptr, world)
-    return PaddedLayout(bounds, max(1, max(bounds[i + 1] - bounds[i] for i in range(world))))
+    max_rows = max(1, max(bounds[i + 1] - bounds[i] for i in range(world)))
+    chunks = max(1, min(int(chunks), max_rows))
+    return PaddedLayout(bounds, -(-max_rows // chunks), chunks)
 
 
-def make_padded_shard(row_ptr: torch.Tensor, col_ind: torch.Tensor, layout: PaddedLayout, rank: int) -> RowShard:
-    """Rank `rank`'s rows with column ids rewritten to padded ids; row_begin is
-    the shard's first padded row (r*max_rows)."""
-    b0, b1 = layout.bounds[rank], layout.bounds[rank + 1]
-    s = make_shard(row_ptr, col_ind, b0, b1)
-    cols = layout.padded_ids(s.col_ind).to(torch.int32)
-    base = rank * layout.max_rows
-    return RowShard(base, base + (b1 - b0), s.row_ptr, cols.contiguous())
+@dataclass
+class PaddedShard:
+    """One rank's rows as `chunks` row pieces with padded column ids."""
+    rank: int
+    pieces: list[RowShard]  # piece c: row_begin = its first padded row, for the dis lookup
+
+    @property
+    def num_rows(self) -> int:
+        return sum(p.num_rows for p in self.pieces)
+
+    @property
+    def num_edges(self) -> int:
+        return sum(p.num_edges for p in self.pieces)
 
 
-def gcn_forward_allgather(shard: RowShard, dis_pad: torch.Tensor, x_pad: torch.Tensor, weights: list[torch.Tensor],
+def make_padded_shard(row_ptr: torch.Tensor, col_ind: torch.Tensor, layout: PaddedLayout, rank: int) -> PaddedShard:
+    """Rank `rank`'s rows cut into the layout's pieces, column ids rewritten to padded ids."""
+    b0 = layout.bounds[rank]
+    pieces = []
+    for c in range(layout.chunks):
+        lo, hi = layout.piece_range(rank, c)
+        s = make_shard(row_ptr, col_ind, b0 + lo, b0 + hi)
+        cols = layout.padded_ids(s.col_ind).to(torch.int32).contiguous() if s.num_edges else s.col_ind
+        first = c * layout.world * layout.chunk_rows + rank * layout.chunk_rows
+        pieces.append(RowShard(first, first + (hi - lo), s.row_ptr, cols))
+    return PaddedShard(rank, pieces)
+
+
+def allgather_buffers(layout: PaddedLayout, feat: int, device) -> dict:
+    """Buffers for gcn_forward_allgather: 'agg' [Mc, F], 'out' [chunks*Mc, F]
+    (padding rows zero), 'x_next' [padded_rows, F]."""
+    return {"agg": torch.empty(layout.chunk_rows, feat, device=device),
+            "out": torch.zeros(layout.local_rows, feat, device=device),
+            "x_next": torch.empty(layout.padded_rows, feat, device=device)}
+
+
+def gcn_forward_allgather(shard: PaddedShard, dis_pad: torch.Tensor, x_pad: torch.Tensor, weights: list[torch.Tensor],
                           biases: list[torch.Tensor], layout: PaddedLayout, bufs: dict, group=None,
                           timers: dict | None = None) -> torch.Tensor:
-    """Multi-layer GCN over a padded-layout shard; one all_gather per layer boundary.
+    """Multi-layer GCN over a padded-layout shard, exchange pipelined by row piece.
 
-    bufs: 'agg' [rows, F], 'out' [max_rows, F] (padding rows zero), 'x_next'
-    [world*max_rows, F]. Returns this rank's [rows, F] output rows.
+    For each piece c: aggregation, X·W + b (+ReLU) into out[c*Mc:...], then an
+    asynchronous all_gather of that piece on the collective stream while the
+    compute stream goes on with piece c+1. The next layer waits for all
+    pieces. Returns this rank's [rows, F] output rows (local order).
     """
     x = x_pad
-    rows = shard.num_rows
     layers = len(weights)
+    mc, world = layout.chunk_rows, layout.world
+    out = bufs["out"]
     for li in range(layers):
-        ev = _mark(timers, "spmm_begin")
-        spmm_gcn_shard(shard, dis_pad, x, bufs["agg"])
-        _mark(timers, "spmm_end", ev)
-        out = bufs["out"]
-        native_ops.linear_forward_(bufs["agg"], weights[li], biases[li], out[:rows], li != layers - 1)
-        if li == layers - 1:
-            return out[:rows]
-        dist.all_gather_into_tensor(bufs["x_next"], out, group=group)
+        last = li == layers - 1
+        works = []
+        for c, piece in enumerate(shard.pieces):
+            lo = c * mc
+            rows_c = piece.num_rows
+            if rows_c:
+                agg = bufs["agg"][:rows_c]
+                ev = _mark(timers, "spmm_begin")
+                spmm_gcn_shard(piece, dis_pad, x, agg)
+                _mark(timers, "spmm_end", ev)
+                native_ops.linear_forward_(agg, weights[li], biases[li], out[lo:lo + rows_c], not last)
+            if not last:
+                works.append(dist.all_gather_into_tensor(bufs["x_next"][c * world * mc:(c + 1) * world * mc],
+                                                         out[lo:lo + mc], group=group, async_op=True))
+        if last:
+            break
+        for w in works:
+            w.wait()
         x = bufs["x_next"]
-    return bufs["out"][:rows]
+    return out[:shard.num_rows]
+
+
+def piece_bounds(row_ptr: np.ndarray, chunks: int) -> list[int]:
+    """Local row boundaries cutting a shard into at most `chunks` non-empty pieces of about equal nnz."""
+    n = int(np.asarray(row_ptr).shape[0]) - 1
+    b = nnz_balanced_bounds(row_ptr, max(1, min(int(chunks), max(n, 1))))
+    out = [b[0]]
+    for v in b[1:]:
+        if v > out[-1]:
+            out.append(v)
+    if len(out) == 1:
+        out.append(n)
+    return out
+
+
+def make_pieces(row_ptr: torch.Tensor, col_ind: torch.Tensor, row_begin: int, row_end: int,
+                chunks: int) -> list[RowShard]:
+    """Rows [row_begin, row_end) as equal-nnz RowShards with global row and column ids."""
+    rp = row_ptr[row_begin:row_end + 1].to(torch.int64).cpu().numpy()
+    b = piece_bounds(rp - rp[0], chunks)
+    return [make_shard(row_ptr, col_ind, row_begin + lo, row_begin + hi) for lo, hi in zip(b[:-1], b[1:])]
+
+
+class _PeerBlock:
+    """Owner of a gnn_peer_alloc buffer exposed through __cuda_array_interface__."""
+
+    def __init__(self, ptr: int, shape, device: int):
+        self.ptr, self.device = ptr, device
+        self.__cuda_array_interface__ = {"shape": tuple(int(s) for s in shape), "typestr": "<f4",
+                                         "data": (ptr, False), "version": 3, "strides": None}
+
+    def free(self):
+        if self.ptr:
+            N.call("gnn_peer_free", ctypes.c_void_p(self.ptr), self.device)
+            self.ptr = 0
+
+
+class PeerRowExchange:
+    """Copy-engine row exchange between the ranks of one node.
+
+    Every rank holds two full [N, F] copies of "the next layer's input" in
+    memory it allocated itself (gnn_peer_alloc) and has mapped every peer's
+    copies through CUDA IPC. A layer writes its output rows straight into the
+    rank's own slice of the current copy; `push` sends a finished row range
+    to the same rows of every peer's current copy, one cudaMemcpyAsync per peer
+    on that peer's copy stream (copy engines over NVLink, no SM), ordered after
+    the producing kernel by an event. `finish` is the device-side barrier: a
+    one-element NCCL all_reduce issued after every push, which the compute
+    stream waits on before reading the copy. Copies alternate per exchange, so
+    a push never lands in a copy that a peer can still be reading: a rank
+    pushes into copy t only after the barrier of the previous exchange, which
+    every peer reaches only after its last read of copy t.
+    """
+
+    def __init__(self, num_rows: int, feat: int, rank: int, world: int, device: torch.device, group=None):
+        self.rank, self.world, self.group = rank, world, group
+        self.device = device
+        self.row_bytes = feat * 4
+        self.shape = (num_rows, feat)
+        dev = device.index
+        nbytes = max(1, num_rows * feat * 4)
+        self._blocks, self.buffers, handles = [], [], []
+        hb = int(N.lib().gnn_ipc_handle_bytes())
+        for _ in range(2):
+            p = ctypes.c_void_p(0)
+            N.call("gnn_peer_alloc", nbytes, dev, ctypes.byref(p))
+            blk = _PeerBlock(p.value, self.shape, dev)
+            self._blocks.append(blk)
+            with torch.cuda.device(dev):
+                self.buffers.append(torch.as_tensor(blk, device=device))
+            h = ctypes.create_string_buffer(hb)
+            N.call("gnn_ipc_get_handle", ctypes.c_void_p(p.value), h, hb)
+            handles.append(h.raw)
+        everyone: list = [None] * world
+        dist.all_gather_object(everyone, handles, group=group)
+        # peer_ptrs[t][p]: peer p's copy t, mapped here
+        self.peer_ptrs: list[dict[int, int]] = [{}, {}]
+        for p in range(world):
+            if p == rank:
+                continue
+            for t in range(2):
+                ptr = ctypes.c_void_p(0)
+                buf = ctypes.create_string_buffer(everyone[p][t], hb)
+                N.call("gnn_ipc_open", buf, hb, dev, ctypes.byref(ptr))
+                self.peer_ptrs[t][p] = ptr.value
+        self.streams = {p: torch.cuda.Stream(device) for p in self.peer_ptrs[0]}
+        self.barrier_stream = torch.cuda.Stream(device)
+        self.flag = torch.zeros(1, device=device)
+        self.turn = 0
+
+    def buffer(self) -> torch.Tensor:
+        """The copy that the current exchange fills."""
+        return self.buffers[self.turn]
+
+    def push(self, row_lo: int, row_hi: int, ready: torch.cuda.Event) -> None:
+        """Send rows [row_lo, row_hi) of the current copy to every peer once `ready` has fired."""
+        if row_hi <= row_lo:
+            return
+        off = row_lo * self.row_bytes
+        nbytes = (row_hi - row_lo) * self.row_bytes
+        src = self.buffers[self.turn].data_ptr() + off
+        for p, s in self.streams.items():
+            s.wait_event(ready)
+            N.call("gnn_copy_async", ctypes.c_void_p(self.peer_ptrs[self.turn][p] + off), ctypes.c_void_p(src),
+                   nbytes, ctypes.c_void_p(s.cuda_stream))
+
+    def finish(self) -> torch.Tensor:
+        """Barrier after every rank's pushes; returns the completed copy and moves to the other one."""
+        for s in self.streams.values():
+            self.barrier_stream.wait_stream(s)
+        with torch.cuda.stream(self.barrier_stream):
+            work = dist.all_reduce(self.flag, group=self.group, async_op=True)
+        work.wait()  # the current (compute) stream waits for the barrier
+        done = self.buffers[self.turn]
+        self.turn ^= 1
+        return done
+
+    def close(self) -> None:
+        """Unmap the peers' copies, then free this rank's copies (all ranks call this)."""
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for t in range(2):
+            for p, ptr in self.peer_ptrs[t].items():
+                N.call("gnn_ipc_close", ctypes.c_void_p(ptr), self.device.index)
+            self.peer_ptrs[t] = {}
+        dist.barrier(group=self.group)
+        self.buffers = []
+        for blk in self._blocks:
+            blk.free()
+        self._blocks = []
+
+
+def gcn_forward_push(pieces: list[RowShard], deg_inv_sqrt: torch.Tensor, x_full: torch.Tensor,
+                     weights: list[torch.Tensor], biases: list[torch.Tensor], exchange: PeerRowExchange,
+                     agg: torch.Tensor, out: torch.Tensor, timers: dict | None = None) -> torch.Tensor:
+    """Multi-layer GCN over this rank's row pieces; layer outputs pushed to the peers piece by piece.
+
+    pieces: this rank's rows as RowShards with global ids (make_pieces), in row
+    order. agg: [max piece rows, F] scratch. out: [rank rows, F] for the last
+    layer. Each piece's aggregation and X·W + b (+ReLU) land in the exchange's
+    current copy, whose rows then go to the peers while the next piece is computed.
+    """
+    layers = len(weights)
+    first = pieces[0].row_begin
+    h = x_full
+    for li in range(layers):
+        last = li == layers - 1
+        dst = out if last else exchange.buffer()
+        base = first if last else 0
+        for piece in pieces:
+            if piece.num_rows == 0:
+                continue
+            a = agg[:piece.num_rows]
+            ev = _mark(timers, "spmm_begin")
+            spmm_gcn_shard(piece, deg_inv_sqrt, h, a)
+            _mark(timers, "spmm_end", ev)
+            native_ops.linear_forward_(a, weights[li], biases[li], dst[piece.row_begin - base:piece.row_end - base],
+                                       not last)
+            if not last:
+                ready = torch.cuda.Event()
+                ready.record()
+                exchange.push(piece.row_begin, piece.row_end, ready)
+        if not last:
+            h = exchange.finish()
+    return out
 
 
 def _mark(timers: dict | None, key: str, begin=None):
-    """Record a CUDA event for per-kernel timing (key 'spmm_begin' / 'spmm_end')."""
+    """Record a CUDA event for per-kernel timing (key 'spmm_begin' / 'spmm_end').
+
+    With several pieces per layer, each piece's aggregation is one entry."""
     if timers is None:
         return None
     ev = torch.cuda.Event(enable_timing=True)

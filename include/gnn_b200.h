@@ -81,10 +81,12 @@ uint64_t gnn_kernel_launches(void);
  * (eligible: 32 <= K <= 256, K % 32 == 0, N % 128 == 0 or N in {32, 64},
  * 16-byte aligned operands). */
 int gnn_gemm_uses_tensor_cores(int64_t m, int64_t k, int64_t n);
-/* Device-side bounded waits (mbarrier spins in the tensor-core kernels) give up
- * after ~2 s instead of hanging; they then record a non-zero code here and the
- * kernel returns early. Synchronises with the current device, stores the word
- * in *status and clears it when reset != 0. */
+/* Device-side bounded waits (mbarrier spins in the tensor-core kernels, the
+ * segment chain of long rows in the aggregation kernels) give up after ~2 s
+ * instead of hanging; they then record a non-zero code here (1-6 tensor-core
+ * pipeline, 16 aggregation segment chain, 17 aggregation long-row list
+ * overflow) and the kernel moves on. Synchronises with the current device,
+ * stores the word in *status and clears it when reset != 0. */
 int gnn_device_status(int reset, int* status);
 
 /* ---- CSR aggregation (SpMM) ------------------------------------------------
@@ -93,8 +95,9 @@ int gnn_device_status(int reset, int* status);
  * into a preallocated `out` of the same shape as `x` ([num_nodes, feat_dim]).
  * Rows of degree <= the long-row threshold are accumulated sequentially in CSR
  * order with fused multiply-adds, exactly like the reference kernels; longer
- * rows are split across the warps of one CTA and the partial sums are added in
- * a fixed order.
+ * rows are cut into segments of long_row_warps * 512 entries, each segment
+ * split across the warps of one CTA, and the partial sums are added in a fixed
+ * order (chunks within a segment, then segments).
  *
  * `workspace` must hold gnn_spmm_workspace_bytes(num_nodes, num_edges) bytes
  * (256-byte aligned, device memory). Two calls in flight at once on different
@@ -131,7 +134,8 @@ int gnn_spmm_gcn_partition_forward(const void* row_ptr, int row_ptr_type, const 
  * 8 MiB (8388608-byte) device array per GPU, held until the process exits.
  * Problems with gnn_spmm_workspace_bytes(num_nodes, num_edges) > 8 MiB are
  * rejected with GNN_ERR_UNSUPPORTED (for example, any graph with at most
- * 2,097,088 nodes fits). All calls on a device share that array: calls that
+ * 1,000,000 nodes and 500,000,000 entries fits, and so does a 2,449,029-node,
+ * 64,308,169-entry graph). All calls on a device share that array: calls that
  * overlap on the GPU race and must be serialised (e.g. one stream). Each call
  * clears the counters it reads. The first call on a device looks the array's
  * address up, so make it before any stream capture on that device. */
@@ -273,6 +277,61 @@ int gnn_pointer_info_query(const void* ptr, gnn_pointer_info* info);
  * pointer itself under HMM, else GNN_ERR_DEVICE. Replaces
  * get_device_accessible_void_ptr, tensor_access.cuh:25-64. */
 int gnn_device_accessible_ptr(const void* host_ptr, void** device_ptr);
+
+/* ---- CSR construction on the device ----------------------------------------
+ * Replaces the host builders of GNN_cuda_common/graph_utils.py:449-535
+ * (build_gcn_normalized_csr, build_pyg_gcn_weighted_csr, build_plain_csr),
+ * which go through scipy's coo_matrix.tocsr() + sort_indices(): rows hold
+ * their distinct columns in increasing order, duplicate pairs merge, and
+ * self-loops (r, r) are appended first when asked. Same arrays bit for bit. */
+
+/* Scratch for gnn_csr_build (two key buffers of num_entries (+ num_nodes) 8-byte
+ * keys plus sort/unique scratch). Queries the current device; 0 on failure. */
+size_t gnn_csr_build_workspace_bytes(int64_t num_entries, int64_t num_nodes, int add_self_loops);
+/* Builds row_ptr [num_nodes + 1] (int32 or int64) and col_ind [*num_unique]
+ * from int64 (row_ids[i], col_ids[i]) pairs, i < num_entries, plus (r, r) for
+ * every node when add_self_loops != 0. col_capacity must be >= the number of
+ * distinct pairs (num_entries + num_nodes always suffices). Ids outside
+ * [0, num_nodes) fail with the host builder's messages ("negative row index
+ * found", "row index exceeds matrix dimensions", ...); an int32 row_ptr fails
+ * when the CSR has more than 2^31 - 1 entries (the reference's cast would wrap).
+ * Synchronises `stream`; *num_unique and *max_degree (largest row length) are
+ * host values on return. */
+int gnn_csr_build(const int64_t* row_ids, const int64_t* col_ids, int64_t num_entries, int64_t num_nodes,
+                  int add_self_loops, void* row_ptr, int row_ptr_type, int32_t* col_ind, int64_t col_capacity,
+                  int64_t* num_unique, int64_t* max_degree, void* workspace, size_t workspace_bytes,
+                  gnn_stream_t stream);
+/* deg_inv_sqrt[r] = table[deg(r)], where table[d] (d = 0..max_degree) holds the
+ * float32 value clip(d, 1)^-0.5 exactly as numpy's float32 power computes it
+ * (graph_utils.py:463-464); the caller fills the table on the host. */
+int gnn_csr_deg_inv_sqrt(const void* row_ptr, int row_ptr_type, int64_t num_nodes, const float* table,
+                         int64_t table_len, float* deg_inv_sqrt, gnn_stream_t stream);
+/* PyG weights edge_weight[e] = deg_inv_sqrt[row(e)] * deg_inv_sqrt[col_ind[e]]
+ * in float32 (graph_utils.py:496-497). */
+int gnn_csr_edge_weight(const void* row_ptr, int row_ptr_type, const int32_t* col_ind, const float* deg_inv_sqrt,
+                        int64_t num_nodes, float* edge_weight, gnn_stream_t stream);
+
+/* ---- peer memory for the row-partitioned multi-GPU mode -------------------- *
+ * No counterpart in the reference, which runs on one GPU. A rank allocates its
+ * copy of the next layer's input with gnn_peer_alloc, exports it with
+ * gnn_ipc_get_handle, opens every peer's copy with gnn_ipc_open, and pushes
+ * each finished row piece into the peers' copies with gnn_copy_async (one
+ * copy-engine transfer per peer; no SM is used). */
+
+/* cudaMalloc(bytes) on `device`, exportable through CUDA IPC. */
+int gnn_peer_alloc(size_t bytes, int device, void** ptr);
+int gnn_peer_free(void* ptr, int device);
+/* Size of an IPC handle (sizeof(cudaIpcMemHandle_t), 64). */
+size_t gnn_ipc_handle_bytes(void);
+/* Writes the IPC handle of a gnn_peer_alloc buffer into `handle`. */
+int gnn_ipc_get_handle(const void* ptr, void* handle, size_t handle_bytes);
+/* Maps a peer's buffer into this process for `device` (peer access enabled lazily). */
+int gnn_ipc_open(const void* handle, size_t handle_bytes, int device, void** ptr);
+int gnn_ipc_close(void* ptr, int device);
+/* *can = cudaDeviceCanAccessPeer(device, peer). */
+int gnn_can_access_peer(int device, int peer, int* can);
+/* cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, stream); 0 bytes is a no-op. */
+int gnn_copy_async(void* dst, const void* src, size_t bytes, gnn_stream_t stream);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

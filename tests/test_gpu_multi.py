@@ -1,4 +1,9 @@
-"""Row-partitioned multi-GPU GCN forward (NCCL) equals the single-GPU forward bit for bit.
+"""Row-partitioned multi-GPU GCN forward equals the single-GPU forward bit for bit.
+
+Covers the three exchanges: NCCL broadcast, NCCL all_gather on the padded
+chunk-major layout (1 and 3 pieces), and copy-engine pushes into the peers'
+IPC-mapped buffers (1 and 3 pieces, three steps in a row so both of the
+alternating buffers are used).
 
 Runs only where at least two GPUs are visible (spawned ranks, one GPU each,
 NCCL with NVLS off). The long-row threshold is fixed so every rank uses the
@@ -56,19 +61,36 @@ def _worker(rank, world, port, q):
         out = partition.gcn_forward_partitioned(shard, dis, x, ws, bs, bounds, rank, bufs)
         full = torch.empty(N_NODES, FEAT, device=dev)
         partition.exchange_rows(out, full, bounds, rank)
-        # padded layout, one all_gather per layer boundary
-        lay = partition.make_padded_layout(rp.cpu().numpy(), world)
-        pshard = partition.make_padded_shard(rp, ci, lay, rank)
-        pbufs = {"agg": torch.empty(pshard.num_rows, FEAT, device=dev),
-                 "out": torch.zeros(lay.max_rows, FEAT, device=dev),
-                 "x_next": torch.empty(lay.padded_rows, FEAT, device=dev)}
-        pout = partition.gcn_forward_allgather(pshard, lay.pad_rows(dis), lay.pad_rows(x), ws, bs, lay, pbufs)
-        pfull = torch.zeros(lay.max_rows, FEAT, device=dev)
-        pfull[:pshard.num_rows] = pout
-        gathered = torch.empty(lay.padded_rows, FEAT, device=dev)
-        dist.all_gather_into_tensor(gathered, pfull)
+        # padded chunk-major layout, pipelined all_gather per row piece
+        padded = []
+        for chunks in (1, 3):
+            lay = partition.make_padded_layout(rp.cpu().numpy(), world, chunks)
+            pshard = partition.make_padded_shard(rp, ci, lay, rank)
+            pbufs = partition.allgather_buffers(lay, FEAT, dev)
+            pout = partition.gcn_forward_allgather(pshard, lay.pad_rows(dis), lay.pad_rows(x), ws, bs, lay, pbufs)
+            # collect the final rows through the same layout
+            pfull = torch.zeros(lay.local_rows, FEAT, device=dev)
+            pfull[:pshard.num_rows] = pout
+            gathered = torch.empty(lay.padded_rows, FEAT, device=dev)
+            for c in range(lay.chunks):
+                mc = lay.chunk_rows
+                dist.all_gather_into_tensor(gathered[c * world * mc:(c + 1) * world * mc], pfull[c * mc:(c + 1) * mc])
+            padded.append(lay.unpad_rows(gathered).cpu().numpy())
+        # copy-engine pushes over IPC mappings, pieces of equal nnz
+        for chunks in (1, 3):
+            pieces = partition.make_pieces(rp, ci, bounds[rank], bounds[rank + 1], chunks)
+            ex = partition.PeerRowExchange(N_NODES, FEAT, rank, world, dev)
+            agg = torch.empty(max(p.num_rows for p in pieces), FEAT, device=dev)
+            mine = torch.empty(rows, FEAT, device=dev)
+            for _ in range(3):  # repeated steps alternate the two copies
+                partition.gcn_forward_push(pieces, dis, x, ws, bs, ex, agg, mine)
+            full_p = torch.empty(N_NODES, FEAT, device=dev)
+            partition.exchange_rows(mine, full_p, bounds, rank)
+            torch.cuda.synchronize(dev)
+            padded.append(full_p.cpu().numpy())
+            ex.close()
         torch.cuda.synchronize(dev)
-        q.put((rank, full.cpu().numpy(), lay.unpad_rows(gathered).cpu().numpy()))
+        q.put((rank, full.cpu().numpy(), padded))
     finally:
         dist.destroy_process_group()
 
@@ -109,4 +131,5 @@ def test_two_gpu_partitioned_gcn_matches_single_gpu():
         assert p.exitcode == 0
     for r in range(2):
         assert np.array_equal(results[r][0].view(np.uint32), single.view(np.uint32)), ("broadcast", r)
-        assert np.array_equal(results[r][1].view(np.uint32), single.view(np.uint32)), ("allgather", r)
+        for k, got in enumerate(results[r][1]):
+            assert np.array_equal(got.view(np.uint32), single.view(np.uint32)), ("allgather", k, r)

@@ -6,6 +6,8 @@ rows follow the documented warp split, which the oracle reproduces with
 ``split_warps`` — so every output element is compared exactly. Every case is
 also held to the north-star fp32 tolerance against float64.
 """
+import ctypes
+
 import numpy as np
 import pytest
 import torch
@@ -286,3 +288,56 @@ def test_long_row_warp_counts():
         out = torch.empty(n, f, device=DEV)
         agg_ops.spmm_sum_forward_(*t, out)
         assert _bits_equal(out.cpu().numpy(), exp), warps
+
+
+def _hub_graph(n: int, hub_degrees, extra: int, seed: int):
+    """Rows 0..len(hub_degrees)-1 are hubs of about the given degrees, plus random pairs."""
+    rng = np.random.default_rng(seed)
+    us, vs = [], []
+    for h, deg in enumerate(hub_degrees):
+        cols = rng.choice(np.arange(len(hub_degrees), n), size=deg, replace=False)
+        us.append(np.full(deg, h))
+        vs.append(cols)
+    us.append(rng.integers(0, n, extra))
+    vs.append(rng.integers(0, n, extra))
+    u = torch.from_numpy(np.concatenate(us).astype(np.int64))
+    v = torch.from_numpy(np.concatenate(vs).astype(np.int64))
+    keep = u != v
+    u, v = u[keep], v[keep]
+    key = torch.unique(torch.minimum(u, v) * n + torch.maximum(u, v))
+    return synth.symmetrize(key // n, key % n)
+
+
+@pytest.mark.parametrize("f", [128, 640])
+def test_multi_segment_hubs_all_kernels(f):
+    """Rows longer than one segment (warps x 512 entries) are summed by several CTAs
+    chained in segment order; every kernel and weight mode matches the oracle bit for bit."""
+    n = 120_000
+    s, d = _hub_graph(n, [100_001, 50_000, 20_000, 9_000, 8_193, 8_192], extra=150_000, seed=21)
+    rp, ci, dis = O.gcn_normalized_csr(s.numpy(), d.numpy(), n)
+    _, _, ew = O.pyg_weighted_csr(s.numpy(), d.numpy(), n)
+    x = synth.features(n, f, seed=22).numpy()
+    assert np.diff(rp).max() > 100_000
+    t = {k: torch.from_numpy(v).to(DEV) for k, v in dict(rp=rp, ci=ci, dis=dis, ew=ew, x=x).items()}
+    old = N.config_get("spmm.kernel")
+    try:
+        for warps in (16, 4):
+            N.config_set("spmm.long_row_warps", warps)
+            N.config_set("spmm.long_row_threshold", 300)
+            exp_gcn = O.spmm(rp, ci, x, mode=O.W_GCN, dis=dis, split_warps=warps, long_thr=300)
+            exp_mean = O.spmm(rp, ci, x, mode=O.W_UNIT, mean=O.M_DIV, split_warps=warps, long_thr=300)
+            for kern in (1, 0, 2):
+                N.config_set("spmm.kernel", kern)
+                o = torch.full((n, f), float("nan"), device=DEV)
+                gcn_ops.spmm_gcn_forward_(t["rp"], t["ci"], t["dis"], t["x"], o)
+                assert _bits_equal(o.cpu().numpy(), exp_gcn), (warps, kern, "gcn")
+                o2 = torch.full((n, f), float("nan"), device=DEV)
+                agg_ops.spmm_mean_forward_(t["rp"], t["ci"], t["x"], o2)
+                assert _bits_equal(o2.cpu().numpy(), exp_mean), (warps, kern, "mean")
+        ref64, ab = O.spmm_f64(rp, ci, x, mode=O.W_GCN, dis=dis)
+        assert O.check_close_to_f64(exp_gcn, ref64, ab) <= 1.0
+    finally:
+        N.config_set("spmm.kernel", old)
+    status = ctypes.c_int(-1)  # no segment gave up waiting for its predecessor
+    N.check(N.lib().gnn_device_status(1, ctypes.byref(status)))
+    assert status.value == 0

@@ -101,3 +101,33 @@ def test_gemm_oracle_close_to_f64():
     ref = O.gemm_f64(x, w, b, True)
     scale = np.abs(x).astype(np.float64) @ np.abs(w).astype(np.float64) + np.abs(b)[None, :]
     assert np.all(np.abs(got - ref) <= 1e-5 * scale + 1e-30)
+
+
+def test_split_rule_segments_and_chunks():
+    """split_warps > 0: long rows are cut into segments of split_warps*512 entries,
+    each cut into split_warps chunks; partials added chunk by chunk, then segment by segment."""
+    from oracle import oracle as O
+    rng = np.random.default_rng(5)
+    n, f, deg = 6000, 3, 5000
+    cols = np.sort(rng.choice(n, size=deg, replace=False)).astype(np.int32)
+    rp = np.array([0, deg] + [deg] * (n - 1), dtype=np.int32)
+    x = rng.standard_normal((n, f)).astype(np.float32)
+    for warps in (4, 16):
+        got = O.spmm(rp, cols, x, mode=O.W_UNIT, split_warps=warps, long_thr=100)[0]
+        seg_len = warps * 512
+        acc = None
+        for sb in range(0, deg, seg_len):
+            se = min(sb + seg_len, deg)
+            chunk = -(-(se - sb) // warps)
+            seg = None
+            for w in range(warps):
+                wb = min(sb + w * chunk, se)
+                we = min(wb + chunk, se)
+                part = np.zeros(f, dtype=np.float32)
+                for e in range(wb, we):
+                    part = (part + x[cols[e]]).astype(np.float32)
+                seg = part if seg is None else (seg + part).astype(np.float32)
+            acc = seg if acc is None else (acc + seg).astype(np.float32)
+        assert np.array_equal(got.view(np.uint32), acc.view(np.uint32)), warps
+        plain = O.spmm(rp, cols, x, mode=O.W_UNIT)[0]
+        assert not np.array_equal(plain.view(np.uint32), got.view(np.uint32)) or warps == 0

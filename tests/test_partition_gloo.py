@@ -2,8 +2,9 @@
 
 The CUDA aggregation is replaced here by the oracle (CPU test only): the test
 covers the host logic of the multi-GPU mode — equal-nnz bounds, shard
-construction with global column ids, and the broadcast-based exchange — and
-checks that the concatenated shard outputs equal the single-rank result bit for bit.
+construction with global column ids, the broadcast-based exchange and the
+padded chunk-major layout with its pipelined all_gather — and checks that the
+exchanged outputs equal the single-rank result bit for bit.
 """
 import os
 import socket
@@ -67,17 +68,63 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
+def test_piece_bounds_and_pieces():
+    rp = np.array([0, 10, 10, 10, 11, 30], dtype=np.int64)
+    for chunks in (1, 2, 3, 5, 9):
+        b = partition.piece_bounds(rp, chunks)
+        assert b[0] == 0 and b[-1] == 5 and all(b[i] < b[i + 1] for i in range(len(b) - 1))
+        assert len(b) - 1 <= chunks
+    assert partition.piece_bounds(np.array([0]), 4) == [0, 0]  # no rows: one empty piece
+    u, v = synth.rmat_undirected(700, 5000, seed=3)
+    s, d = synth.symmetrize(u, v)
+    from gnn_cuda_b200.GNN_cuda_common import graph_utils as G
+    g = G.build_gcn_normalized_csr(s, d, num_nodes=700)
+    pieces = partition.make_pieces(g.row_ptr, g.col_ind, 100, 650, 4)
+    assert pieces[0].row_begin == 100 and pieces[-1].row_end == 650
+    assert all(a.row_end == b.row_begin for a, b in zip(pieces[:-1], pieces[1:]))
+    cols = torch.cat([p.col_ind for p in pieces])
+    assert torch.equal(cols, g.col_ind[g.row_ptr[100]:g.row_ptr[650]])  # global ids, CSR order kept
+    for p in pieces:
+        assert int(p.row_ptr[0]) == 0 and int(p.row_ptr[-1]) == p.num_edges
+
+
 def test_padded_layout_maps():
     rp = np.array([0, 3, 3, 10, 12, 20, 21, 30], dtype=np.int64)  # 7 rows
     lay = partition.make_padded_layout(rp, 3)
     assert lay.bounds[0] == 0 and lay.bounds[-1] == 7 and lay.world == 3
     g = torch.arange(7)
     p = lay.padded_ids(g)
-    assert torch.all(p[1:] > p[:-1])  # increasing: CSR column order survives the remap
+    assert torch.all(p[1:] > p[:-1])  # one piece: the plain r*Mc + i layout, increasing
     x = torch.arange(7 * 2, dtype=torch.float32).view(7, 2)
     xp = lay.pad_rows(x)
     assert xp.shape == (lay.padded_rows, 2)
     assert torch.equal(xp[p], x) and torch.equal(lay.unpad_rows(xp), x)
+
+
+@pytest.mark.parametrize("world,chunks", [(2, 3), (3, 2), (4, 5), (2, 64)])
+def test_padded_layout_chunk_major(world, chunks):
+    u, v = synth.rmat_undirected(300, 2000, seed=world + chunks)
+    s, d = synth.symmetrize(u, v)
+    from gnn_cuda_b200.GNN_cuda_common import graph_utils as G
+    g = G.build_gcn_normalized_csr(s, d, num_nodes=300)
+    lay = partition.make_padded_layout(g.row_ptr.numpy(), world, chunks)
+    ids = lay.padded_ids(torch.arange(300))
+    assert len(set(ids.tolist())) == 300 and int(ids.max()) < lay.padded_rows  # injective, in range
+    mc = lay.chunk_rows
+    for r in range(world):
+        for c in range(lay.chunks):
+            lo, hi = lay.piece_range(r, c)
+            got = ids[lay.bounds[r] + lo:lay.bounds[r] + hi]
+            want = c * world * mc + r * mc + torch.arange(hi - lo)
+            assert torch.equal(got, want)  # piece c of rank r is one contiguous block
+    # the pieces' rows and entries add up to the shard
+    sh = partition.make_padded_shard(g.row_ptr, g.col_ind, lay, 1)
+    b0, b1 = lay.bounds[1], lay.bounds[2]
+    assert sh.num_rows == b1 - b0 and sh.num_edges == int(g.row_ptr[b1] - g.row_ptr[b0])
+    cols = torch.cat([p.col_ind.to(torch.int64) for p in sh.pieces])
+    assert torch.equal(cols, ids[g.col_ind[g.row_ptr[b0]:g.row_ptr[b1]].to(torch.int64)])
+    x = torch.randn(300, 3)
+    assert torch.equal(lay.unpad_rows(lay.pad_rows(x)), x)
 
 
 def _worker_padded(rank, world, port, q):
@@ -91,20 +138,31 @@ def _worker_padded(rank, world, port, q):
         s, d = synth.symmetrize(u, v)
         g = G.build_gcn_normalized_csr(s, d, num_nodes=n)
         x = synth.features(n, f, seed=8)
-        lay = partition.make_padded_layout(g.row_ptr.numpy(), world)
-        shard = partition.make_padded_shard(g.row_ptr, g.col_ind, lay, rank)
-        dis_pad = lay.pad_rows(g.deg_inv_sqrt)
-        x_pad = lay.pad_rows(x)
-        rp_local = shard.row_ptr.numpy()
-        rows = np.repeat(np.arange(shard.num_rows) + shard.row_begin, np.diff(rp_local))
-        cols = shard.col_ind.numpy()
-        ew = (dis_pad.numpy()[rows] * dis_pad.numpy()[cols]).astype(np.float32)
-        out_local = O.spmm(rp_local, cols, x_pad.numpy(), mode=O.W_EDGE, ew=ew)
-        out = torch.zeros(lay.max_rows, f)
-        out[:shard.num_rows] = torch.from_numpy(out_local)
-        gathered = torch.empty(lay.padded_rows, f)
-        dist.all_gather_into_tensor(gathered, out)
-        q.put((rank, lay.unpad_rows(gathered).numpy()))
+        results = []
+        for chunks in (1, 4):
+            lay = partition.make_padded_layout(g.row_ptr.numpy(), world, chunks)
+            shard = partition.make_padded_shard(g.row_ptr, g.col_ind, lay, rank)
+            dis_pad = lay.pad_rows(g.deg_inv_sqrt).numpy()
+            x_pad = lay.pad_rows(x).numpy()
+            out = torch.zeros(lay.local_rows, f)
+            gathered = torch.empty(lay.padded_rows, f)
+            works = []
+            mc = lay.chunk_rows
+            # per piece: aggregate its rows (oracle, CPU test only), then start its exchange
+            for c, piece in enumerate(shard.pieces):
+                if piece.num_rows:
+                    rp_local = piece.row_ptr.numpy()
+                    rows = np.repeat(np.arange(piece.num_rows) + piece.row_begin, np.diff(rp_local))
+                    cols = piece.col_ind.numpy()
+                    ew = (dis_pad[rows] * dis_pad[cols]).astype(np.float32)
+                    out[c * mc:c * mc + piece.num_rows] = torch.from_numpy(
+                        O.spmm(rp_local, cols, x_pad, mode=O.W_EDGE, ew=ew))
+                works.append(dist.all_gather_into_tensor(gathered[c * world * mc:(c + 1) * world * mc],
+                                                         out[c * mc:(c + 1) * mc], async_op=True))
+            for w in works:
+                w.wait()
+            results.append(lay.unpad_rows(gathered).numpy())
+        q.put((rank, results))
     finally:
         dist.destroy_process_group()
 
@@ -129,7 +187,8 @@ def test_two_rank_padded_allgather_matches_single_rank():
     x = synth.features(n, f, seed=8)
     ref = O.spmm(g.row_ptr.numpy(), g.col_ind.numpy(), x.numpy(), mode=O.W_GCN, dis=g.deg_inv_sqrt.numpy())
     for r in range(2):
-        assert np.array_equal(results[r].view(np.uint32), ref.view(np.uint32))
+        for got in results[r]:
+            assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
 
 
 def test_two_rank_exchange_matches_single_rank():

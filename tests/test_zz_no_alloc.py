@@ -82,4 +82,6 @@ def test_noalloc_refuses_problems_beyond_its_scratch():
     assert rc == 3  # GNN_ERR_UNSUPPORTED
     msg = N.last_error()
     assert "8388608" in msg and "gnn_spmm_gcn_forward with a workspace" in msg
-    assert L.gnn_spmm_workspace_bytes(2_097_088, 10**9) == 8 << 20  # the documented largest node count fits
+    # the documented examples fit
+    assert L.gnn_spmm_workspace_bytes(1_000_000, 500_000_000) <= 8 << 20
+    assert L.gnn_spmm_workspace_bytes(2_449_029, 64_308_169) <= 8 << 20
