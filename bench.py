@@ -321,7 +321,7 @@ def run_ours(args, rank: int, world: int, device: torch.device):
         "data": f"synthetic: seeded R-MAT graph (seed {args.seed}) with ogbn-products shape, N(0,1) features, "
                 "Glorot weights, zero bias",
         "config": describe(prob, world, chunks=args.chunks, exchange=args.exchange),
-        "roofline": {"bound": "hbm", "kernel": "spmm_vec_kernel (GCN aggregation)",
+        "roofline": {"bound": "hbm", "kernel": "spmm_vec_kernel + spmm_long_kernel (GCN aggregation)",
                      "achieved": round(achieved, 1) if achieved else None, "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4) if achieved else None, "peak_source": peak_kind,
                      "spmm_ms_per_layer": round(spmm_ms_avg, 4), "algorithmic_bytes_per_layer": shard_bytes,

@@ -33,6 +33,7 @@
 #include <stdint.h>
 
 #include <algorithm>
+#include <mutex>
 #include <string>
 
 #include "common.cuh"
@@ -80,6 +81,18 @@ constexpr uint32_t kSegTag = 0x80000000u;
 #endif
 #ifndef GNN_SPMM_MIN_BLOCKS
 #define GNN_SPMM_MIN_BLOCKS 3  // at F <= 128 (one float4 per lane); wider rows keep 2
+#endif
+// Long-row kernel (spmm_long_kernel): register budget, grid and gather depth.
+// Measured on B200 (products-shaped graph, F = 128): 64 registers and one
+// full wave of long CTAs (2 per SM) beat 40 registers or 1 CTA per SM by 12-30 %.
+#ifndef GNN_SPMM_LONG_MIN_BLOCKS
+#define GNN_SPMM_LONG_MIN_BLOCKS 2  // register budget: 64 per thread at 512 threads
+#endif
+#ifndef GNN_SPMM_LONG_CTAS_PER_SM
+#define GNN_SPMM_LONG_CTAS_PER_SM 2  // grid size: one full wave; per-row CTAs fill SMs as long CTAs finish
+#endif
+#ifndef GNN_SPMM_LONG_U
+#define GNN_SPMM_LONG_U 4  // neighbour rows in flight per warp in the long-row kernel (F <= 128)
 #endif
 template <int NV>
 __host__ __device__ constexpr int gather_depth() {
@@ -297,10 +310,21 @@ __device__ __forceinline__ bool wait_at_least(const uint32_t* p, uint32_t target
 // stored, and adds its partial to the stored prefix: row = ((s0 + s1) + s2)...
 // Tickets are handed out in unit order, so a waiting segment's predecessors
 // were taken earlier by CTAs that are running; the wait always ends.
-// Out of line by default: the long-row phase then gets its own register
-// allocation and does not raise the pressure (and spills) of the per-row path.
+// Inlined by default. Measured on B200 (products-shaped graph, F = 128): out of
+// line, the phase gets its own register allocation but the call costs the
+// per-row path more (5.65 vs 5.45 ms per aggregation). The kernels take their
+// arguments as __grid_constant__, so an out-of-line phase reads them in place
+// through a reference instead of from a per-thread local copy.
 #ifndef GNN_SPMM_LONG_NOINLINE
-#define GNN_SPMM_LONG_NOINLINE 1
+#define GNN_SPMM_LONG_NOINLINE 0
+#endif
+#ifndef GNN_SPMM_GRID_CONST
+#define GNN_SPMM_GRID_CONST 1
+#endif
+#if GNN_SPMM_GRID_CONST
+#define GNN_KPARAM const __grid_constant__
+#else
+#define GNN_KPARAM
 #endif
 #if GNN_SPMM_LONG_NOINLINE
 #define GNN_LONG_PHASE_INLINE __noinline__
@@ -309,7 +333,7 @@ __device__ __forceinline__ bool wait_at_least(const uint32_t* p, uint32_t target
 #endif
 template <int WM, int MEAN, bool HOT, int NV, class IdxT>
 __device__ GNN_LONG_PHASE_INLINE void long_rows_phase(const SpmmArgs& a, float4* s_part, uint32_t* s_ticket) {
-  constexpr int U = gather_depth<NV>();
+  constexpr int U = NV == 1 ? GNN_SPMM_LONG_U : gather_depth<NV>();
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int nwarps = blockDim.x >> 5;
@@ -335,58 +359,60 @@ __device__ GNN_LONG_PHASE_INLINE void long_rows_phase(const SpmmArgs& a, float4*
     if (t >= total) break;
     const uint32_t unit = t / tiles;
     const int tile = static_cast<int>(t - unit * tiles);
-    int64_t r, k = 0, nk = 1;
-    uint32_t head = 0;
+    // Index arithmetic stays in the row_ptr type (32-bit for int32 row_ptr):
+    // this phase shares the kernel's register budget with the per-row path.
+    int r;  // row ids fit int32 (num_nodes is limited to int32 column ids)
+    uint32_t k = 0, head = unit;
     if (unit < nseg) {
       const uint2 it = __ldcg(a.seg_items + unit);  // a head's .y may already count stored units
-      r = it.x;
-      k = (it.y & kSegTag) ? (it.y & ~kSegTag) : 0;
-      head = unit - static_cast<uint32_t>(k);
+      r = static_cast<int>(it.x);
+      k = (it.y & kSegTag) ? (it.y & ~kSegTag) : 0u;
+      head = unit - k;
     } else {
-      r = a.long_list[unit - nseg];
+      r = static_cast<int>(a.long_list[unit - nseg]);
     }
     const IdxT beg = rp[r];
     const IdxT end = rp[r + 1];
-    const int64_t deg = static_cast<int64_t>(end - beg);
-    if (unit < nseg) nk = (deg + a.seg_len - 1) / a.seg_len;
-    const int64_t sb = static_cast<int64_t>(beg) + k * a.seg_len;
-    const int64_t se = min(sb + a.seg_len, static_cast<int64_t>(end));
-    const int64_t chunk = (se - sb + split - 1) / split;
+    const IdxT seg = static_cast<IdxT>(a.seg_len);
+    const IdxT sb = beg + static_cast<IdxT>(k) * seg;
+    const IdxT se = (end - sb > seg) ? static_cast<IdxT>(sb + seg) : end;
+    const bool last = se == end;  // the row's final segment (or its only one)
+    const IdxT chunk = (se - sb + split - 1) / split;
     const int64_t col0 = static_cast<int64_t>(tile) * kTileF4 + lane;
     bool valid[NV];
 #pragma unroll
     for (int q = 0; q < NV; ++q) valid[q] = (col0 + 32 * q) < f4;
     const float rs = (WM == kGcn) ? __ldg(a.dis_row + r) : 1.0f;
     for (int c = warp; c < split; c += nwarps) {
-      const int64_t wb = min(sb + c * chunk, se);
-      const int64_t we = min(wb + chunk, se);
+      const IdxT off = static_cast<IdxT>(c) * chunk;
+      const IdxT wb = off < se - sb ? static_cast<IdxT>(sb + off) : se;
+      const IdxT we = se - wb > chunk ? static_cast<IdxT>(wb + chunk) : se;
       float4 acc[NV];
 #pragma unroll
       for (int q = 0; q < NV; ++q) acc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
-      accumulate_edges<WM, HOT, NV, U, IdxT>(a, static_cast<IdxT>(wb), static_cast<IdxT>(we), rs, lane, col0,
-                                             valid, acc);
+      accumulate_edges<WM, HOT, NV, U, IdxT>(a, wb, we, rs, lane, col0, valid, acc);
 #pragma unroll
       for (int q = 0; q < NV; ++q) s_part[c * 32 * NV + q * 32 + lane] = acc[q];
     }
     __syncthreads();
     if (k > 0) {
-      if (threadIdx.x == 0 && !wait_at_least(&a.seg_items[head].y, static_cast<uint32_t>(k) * tiles)) {
+      if (threadIdx.x == 0 && !wait_at_least(&a.seg_items[head].y, k * tiles)) {
         atomicCAS(&g_spmm_status, 0, kChainTimeout);
       }
       __syncthreads();
     }
-    float4* orow = reinterpret_cast<float4*>(a.out + r * a.f);
+    float4* orow = reinterpret_cast<float4*>(a.out + static_cast<int64_t>(r) * a.f);
     for (int j = threadIdx.x; j < 32 * NV; j += blockDim.x) {
       const int64_t cj = static_cast<int64_t>(tile) * kTileF4 + j;
       if (cj < f4) {
         float4 s = s_part[j];
         for (int w = 1; w < split; ++w) s = add4(s, s_part[w * 32 * NV + j]);
         if (k > 0) s = add4(__ldcg(orow + cj), s);
-        if (k == nk - 1) s = finish<MEAN>(s, deg);
+        if (last) s = finish<MEAN>(s, static_cast<int64_t>(end - beg));
         orow[cj] = s;
       }
     }
-    if (k < nk - 1) {
+    if (!last) {
       __threadfence();
       __syncthreads();
       if (threadIdx.x == 0) atomicAdd(&a.seg_items[head].y, 1u);
@@ -395,14 +421,24 @@ __device__ GNN_LONG_PHASE_INLINE void long_rows_phase(const SpmmArgs& a, float4*
   }
 }
 
-// Main vector kernel. Blocks [0, num_long_blocks) serve the long-row list;
-// the rest take kRowsPerWarp rows per warp, skipping long rows.
+// Long rows of the per-row path, in a kernel of their own: it runs beside
+// spmm_vec_kernel (forked onto a side stream and joined back), so the hubs
+// are summed while the short rows stream, and neither kernel's register
+// allocation is shaped by the other's code.
+template <int WM, int MEAN, bool HOT, int NV, class IdxT>
+__global__ void __launch_bounds__(kBlockThreads, GNN_SPMM_LONG_MIN_BLOCKS)
+    spmm_long_kernel(GNN_KPARAM SpmmArgs a) {
+  extern __shared__ float4 s_part[];  // [long_split][32 * NV]
+  __shared__ uint32_t s_ticket;
+  long_rows_phase<WM, MEAN, HOT, NV, IdxT>(a, s_part, &s_ticket);
+}
+
+// Per-row vector kernel: kRowsPerWarp rows per warp, skipping long rows
+// (spmm_long_kernel's).
 template <int WM, int MEAN, bool HOT, int NV, class IdxT>
 __global__ void __launch_bounds__(kBlockThreads, resident_blocks<NV>())
-    spmm_vec_kernel(SpmmArgs a, int num_long_blocks) {
+    spmm_vec_kernel(GNN_KPARAM SpmmArgs a) {
   constexpr int U = gather_depth<NV>();
-  extern __shared__ float4 s_part[];  // [nwarps][32 * NV] (long rows only)
-  __shared__ uint32_t s_ticket;
 
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -415,18 +451,12 @@ __global__ void __launch_bounds__(kBlockThreads, resident_blocks<NV>())
   for (int q = 0; q < NV; ++q) valid[q] = (col0 + 32 * q) < f4;
   const IdxT* __restrict__ rp = static_cast<const IdxT*>(a.row_ptr);
 
-  if (static_cast<int>(blockIdx.x) < num_long_blocks) {
-    // ---- long rows and their segments, split across all warps ----
-    long_rows_phase<WM, MEAN, HOT, NV, IdxT>(a, s_part, &s_ticket);
-    return;
-  }
-
   // ---- normal rows ----
   // Lane i (< kRowsPerWarp) fetches row i's bounds and scale once; the first
   // 32-edge chunk (columns + weights) of row i+1 is loaded while row i's
   // neighbour rows are being gathered, so a row does not start with a
   // row_ptr -> col_ind -> gather chain of dependent loads.
-  const int64_t blk = static_cast<int64_t>(blockIdx.x) - num_long_blocks;
+  const int64_t blk = blockIdx.x;
   int my_row = -1;  // row ids fit int32 (num_nodes is limited to int32 column ids)
   IdxT my_beg = 0, my_end = 0;
   float my_rs = 1.0f;
@@ -495,7 +525,7 @@ __global__ void __launch_bounds__(kBlockThreads, resident_blocks<NV>())
 // low-degree rows no longer leave lanes idle or serialise a row_ptr -> col ->
 // gather latency chain per row, and no warp waits for slower rows of its block.
 template <int WM, int MEAN, bool HOT, int NV, class IdxT>
-__global__ void __launch_bounds__(kBlockThreads, resident_blocks<NV>()) spmm_stream_kernel(SpmmArgs a) {
+__global__ void __launch_bounds__(kBlockThreads, resident_blocks<NV>()) spmm_stream_kernel(GNN_KPARAM SpmmArgs a) {
   constexpr int U = gather_depth<NV>();
   extern __shared__ float4 s_part[];  // [nwarps][32 * NV] (long rows only)
   __shared__ uint32_t s_ticket;
@@ -658,7 +688,7 @@ __device__ __forceinline__ void cp_async_wait() {
 }
 
 template <int WM, int MEAN, bool HOT, int NV, class IdxT>
-__global__ void __launch_bounds__(384, 1) spmm_async_kernel(SpmmArgs a) {
+__global__ void __launch_bounds__(384, 1) spmm_async_kernel(GNN_KPARAM SpmmArgs a) {
   extern __shared__ float4 s_dyn[];
   __shared__ uint32_t s_ticket;
   constexpr int kRowF4 = 32 * NV;                                 // float4 slots per staged row
@@ -908,6 +938,33 @@ int64_t resolve_long_threshold(int64_t n, int64_t nnz) {
   return std::max(thr, kMinLongThreshold);
 }
 
+// Per-device side stream (non-blocking, so it never synchronises implicitly
+// with the legacy default stream) and the fork / join events of the long-row
+// kernel. The mutex keeps one call's record / wait pairs together when several
+// host threads use the same device.
+struct SideStream {
+  cudaStream_t stream = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+  std::mutex mu;
+};
+
+int side_stream(SideStream** out) {
+  static SideStream table[64];
+  static std::mutex init_mu;
+  int dev = 0;
+  GNN_CUDA_TRY(cudaGetDevice(&dev), "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(GNN_ERR_UNSUPPORTED, "spmm: device index above 63");
+  SideStream& s = table[dev];
+  std::lock_guard<std::mutex> g(init_mu);
+  if (s.stream == nullptr) {
+    GNN_CUDA_TRY(cudaStreamCreateWithFlags(&s.stream, cudaStreamNonBlocking), "spmm: create side stream");
+    GNN_CUDA_TRY(cudaEventCreateWithFlags(&s.fork, cudaEventDisableTiming), "spmm: create fork event");
+    GNN_CUDA_TRY(cudaEventCreateWithFlags(&s.join, cudaEventDisableTiming), "spmm: create join event");
+  }
+  *out = &s;
+  return GNN_OK;
+}
+
 template <int WM, int MEAN, bool HOT, class IdxT>
 int launch_vec(SpmmArgs a, cudaStream_t stream) {
   const int64_t f4 = a.f >> 2;
@@ -923,25 +980,66 @@ int launch_vec(SpmmArgs a, cudaStream_t stream) {
   dim3 block(threads);
 
   if (config().spmm_kernel.load() == 1) {
-    // per-row kernel: one warp per row, blocks of consecutive rows
-    int num_long_blocks = 0;
-    if (a.long_cap > 0) {
-      num_long_blocks = static_cast<int>(std::min<int64_t>(a.long_cap + a.seg_cap, 2 * sm_count()));
-    }
-    const int64_t gx = normal_blocks + num_long_blocks;
+    // per-row kernel: one warp per row, blocks of consecutive rows; long rows
+    // in spmm_long_kernel on the device's side stream, forked from and joined
+    // back to `stream`
+    const int64_t gx = normal_blocks;
     if (gx > 0x7fffffffLL) return fail(GNN_ERR_UNSUPPORTED, "spmm: too many rows for one launch");
-    dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(tiles));
+    SideStream* side = nullptr;
+    if (a.long_cap > 0) {
+      int rc = side_stream(&side);
+      if (rc != GNN_OK) return rc;
+      side->mu.lock();
+      const int long_blocks = static_cast<int>(
+          std::min<int64_t>(a.long_cap + a.seg_cap, static_cast<int64_t>(GNN_SPMM_LONG_CTAS_PER_SM) * sm_count()));
+      const size_t long_smem = static_cast<size_t>(a.long_split) * 32 * nv * sizeof(float4);
+      cudaError_t e = cudaEventRecord(side->fork, stream);
+      if (e == cudaSuccess) e = cudaStreamWaitEvent(side->stream, side->fork, 0);
+      if (e != cudaSuccess) {
+        side->mu.unlock();
+        return fail(GNN_ERR_CUDA, std::string("spmm: fork to side stream: ") + cudaGetErrorString(e));
+      }
+      dim3 lgrid(static_cast<unsigned>(long_blocks), static_cast<unsigned>(tiles));
 #define GNN_LAUNCH_NV(NVV) \
-  spmm_vec_kernel<WM, MEAN, HOT, NVV, IdxT><<<grid, block, smem, stream>>>(a, num_long_blocks)
-    switch (nv) {
-      case 1: GNN_LAUNCH_NV(1); break;
-      case 2: GNN_LAUNCH_NV(2); break;
-      case 3: GNN_LAUNCH_NV(3); break;
-      default: GNN_LAUNCH_NV(4); break;
-    }
+  spmm_long_kernel<WM, MEAN, HOT, NVV, IdxT><<<lgrid, block, long_smem, side->stream>>>(a)
+      switch (nv) {
+        case 1: GNN_LAUNCH_NV(1); break;
+        case 2: GNN_LAUNCH_NV(2); break;
+        case 3: GNN_LAUNCH_NV(3); break;
+        default: GNN_LAUNCH_NV(4); break;
+      }
 #undef GNN_LAUNCH_NV
-    GNN_LAUNCH_CHECK("spmm kernel launch");
-    return GNN_OK;
+      e = cudaGetLastError();
+      if (e == cudaSuccess) e = cudaEventRecord(side->join, side->stream);
+      if (e != cudaSuccess) {
+        side->mu.unlock();
+        return fail(GNN_ERR_CUDA, std::string("spmm long-row kernel launch: ") + cudaGetErrorString(e));
+      }
+      count_launch();
+    }
+    int rc = GNN_OK;
+    if (gx > 0) {
+      dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(tiles));
+#define GNN_LAUNCH_NV(NVV) spmm_vec_kernel<WM, MEAN, HOT, NVV, IdxT><<<grid, block, 0, stream>>>(a)
+      switch (nv) {
+        case 1: GNN_LAUNCH_NV(1); break;
+        case 2: GNN_LAUNCH_NV(2); break;
+        case 3: GNN_LAUNCH_NV(3); break;
+        default: GNN_LAUNCH_NV(4); break;
+      }
+#undef GNN_LAUNCH_NV
+      const cudaError_t e = cudaGetLastError();
+      if (e != cudaSuccess) rc = fail(GNN_ERR_CUDA, std::string("spmm kernel launch: ") + cudaGetErrorString(e));
+      else count_launch();
+    }
+    if (side != nullptr) {
+      const cudaError_t e = cudaStreamWaitEvent(stream, side->join, 0);  // join, also on the error path
+      side->mu.unlock();
+      if (e != cudaSuccess && rc == GNN_OK) {
+        rc = fail(GNN_ERR_CUDA, std::string("spmm: join side stream: ") + cudaGetErrorString(e));
+      }
+    }
+    return rc;
   }
 
   if (config().spmm_kernel.load() == 2) {
