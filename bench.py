@@ -197,7 +197,7 @@ def run_ours(args, rank: int, world: int, device: torch.device):
                 "out1": torch.empty(n, FEAT, device=device)}
     elif args.exchange == "push":
         # equal-nnz row ranges cut into pieces; each piece's output is pushed to the peers as it finishes
-        bounds = partition.nnz_balanced_bounds(rp_cpu, world)
+        bounds = partition.nnz_balanced_bounds(rp_cpu, world, partition.ROW_COST_IN_ENTRIES)
         pieces = partition.make_pieces(prob["rp"], prob["ci"], bounds[rank], bounds[rank + 1], args.chunks)
         shard = partition.PaddedShard(rank, pieces)  # used for its row / entry counts
         del prob["rp"], prob["ci"]

@@ -10,6 +10,7 @@
 // runs at the same time.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstring>
 #include <string>
 
@@ -112,6 +113,57 @@ extern "C" int gnn_copy_async(void* dst, const void* src, size_t bytes, gnn_stre
   GNN_REQUIRE(dst != nullptr && src != nullptr, GNN_ERR_NULL_POINTER, "dst and src must not be NULL");
   GNN_CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, static_cast<cudaStream_t>(stream)),
                "cudaMemcpyAsync");
+  clear_error();
+  return GNN_OK;
+}
+
+namespace {
+
+constexpr int kMaxPeers = 8;
+
+struct PeerTargets {
+  char* dst[kMaxPeers];
+};
+
+// Reads each 16-byte word of src once and stores it into every target (peer
+// buffers mapped through CUDA IPC): the SMs drive the NVLink writes.
+__global__ void __launch_bounds__(512) push_rows_kernel(const int4* __restrict__ src, PeerTargets t, int ntargets,
+                                                        int64_t words) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < words; i += stride) {
+    const int4 v = __ldg(src + i);
+#pragma unroll
+    for (int p = 0; p < kMaxPeers; ++p) {
+      if (p < ntargets) reinterpret_cast<int4*>(t.dst[p])[i] = v;
+    }
+  }
+}
+
+}  // namespace
+
+extern "C" int gnn_peer_push(const void* src, void* const* dsts, int ndst, size_t bytes, int ctas,
+                             gnn_stream_t stream) {
+  if (bytes == 0 || ndst == 0) {
+    clear_error();
+    return GNN_OK;
+  }
+  GNN_REQUIRE(src != nullptr && dsts != nullptr, GNN_ERR_NULL_POINTER, "src and dsts must not be NULL");
+  GNN_REQUIRE(ndst > 0 && ndst <= kMaxPeers, GNN_ERR_INVALID_ARGUMENT,
+              "ndst must be in 1.." + std::to_string(kMaxPeers));
+  GNN_REQUIRE(bytes % 16 == 0 && reinterpret_cast<uintptr_t>(src) % 16 == 0, GNN_ERR_INVALID_ARGUMENT,
+              "bytes and src must be multiples of 16");
+  PeerTargets t{};
+  for (int p = 0; p < ndst; ++p) {
+    GNN_REQUIRE(dsts[p] != nullptr && reinterpret_cast<uintptr_t>(dsts[p]) % 16 == 0, GNN_ERR_INVALID_ARGUMENT,
+                "every destination must be a 16-byte aligned, non-NULL pointer");
+    t.dst[p] = static_cast<char*>(dsts[p]);
+  }
+  const int64_t words = static_cast<int64_t>(bytes / 16);
+  const int64_t want = (words + 511) / 512;
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, ctas > 0 ? ctas : 4 * sm_count())));
+  push_rows_kernel<<<grid, 512, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<const int4*>(src), t, ndst,
+                                                                       words);
+  GNN_LAUNCH_CHECK("peer push kernel launch");
   clear_error();
   return GNN_OK;
 }

@@ -2,8 +2,9 @@
 
 SpMM rows are independent given the full input matrix, so rows shard with no
 communication inside a layer. Each rank owns a contiguous row range chosen so
-every rank holds about the same number of CSR entries (power-law graphs make
-equal-row splits badly unbalanced), keeps the full feature matrix, and after
+every rank carries about the same aggregation cost — its CSR entries plus a
+measured per-row cost (power-law graphs make equal-row splits badly
+unbalanced) — keeps the full feature matrix, and after
 every layer except the last the ranks exchange their output rows so everyone
 again holds the full [N, F] input of the next layer.
 
@@ -30,13 +31,23 @@ from . import _native as N
 from .GNN_cuda_common import native_ops
 
 
-def nnz_balanced_bounds(row_ptr: np.ndarray, world: int) -> list[int]:
-    """Row boundaries b[0]=0 < ... < b[world]=n with about nnz/world entries per range."""
+# Aggregation cost of one row relative to one CSR entry, for balancing ranks:
+# measured on B200 with the products-shaped GCN (F = 128) split into two
+# equal-entry shards, time = a * entries + b * rows gives b / a ~ 6 (each row
+# also writes a 512-byte output row and reads its bounds and scale).
+ROW_COST_IN_ENTRIES = 6
+
+
+def nnz_balanced_bounds(row_ptr: np.ndarray, world: int, row_cost: float = 0.0) -> list[int]:
+    """Row boundaries b[0]=0 <= ... <= b[world]=n giving every range about the same
+    cost, where a range costs its CSR entries + row_cost * its rows (row_cost 0:
+    equal entries)."""
     row_ptr = np.asarray(row_ptr, dtype=np.int64)
     n = row_ptr.shape[0] - 1
-    nnz = int(row_ptr[-1])
-    targets = [(nnz * r) // world for r in range(1, world)]
-    inner = [int(np.searchsorted(row_ptr, t, side="left")) for t in targets]
+    cost = row_ptr.astype(np.float64) + float(row_cost) * np.arange(n + 1, dtype=np.float64)
+    total = float(cost[-1])
+    targets = [total * r / world for r in range(1, world)]
+    inner = [int(np.searchsorted(cost, t, side="left")) for t in targets]
     bounds = [0] + [min(max(b, 0), n) for b in inner] + [n]
     for i in range(1, len(bounds)):  # monotone even when one row holds more than a share
         bounds[i] = max(bounds[i], bounds[i - 1])

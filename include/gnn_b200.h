@@ -332,6 +332,11 @@ int gnn_ipc_close(void* ptr, int device);
 int gnn_can_access_peer(int device, int peer, int* can);
 /* cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, stream); 0 bytes is a no-op. */
 int gnn_copy_async(void* dst, const void* src, size_t bytes, gnn_stream_t stream);
+/* One kernel that reads [src, src + bytes) once and stores it to each of the
+ * ndst (<= 8) destinations (peer buffers from gnn_ipc_open): the SMs drive the
+ * NVLink writes. ctas limits the grid (0 = 4 per SM). bytes, src and every
+ * destination must be 16-byte aligned. */
+int gnn_peer_push(const void* src, void* const* dsts, int ndst, size_t bytes, int ctas, gnn_stream_t stream);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

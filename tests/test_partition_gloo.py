@@ -29,6 +29,12 @@ def test_bounds_balance_nnz():
         assert b[0] == 0 and b[-1] == 5000 and all(b[i] <= b[i + 1] for i in range(world))
         loads = [rp[b[i + 1]] - rp[b[i]] for i in range(world)]
         assert max(loads) - min(loads) <= rp[1:].max() - rp[:-1].min() + np.diff(rp).max() * 2
+    # with a per-row cost, ranges balance entries + row_cost * rows
+    for world in (2, 4, 8):
+        b = partition.nnz_balanced_bounds(rp, world, row_cost=6)
+        costs = [rp[b[i + 1]] - rp[b[i]] + 6 * (b[i + 1] - b[i]) for i in range(world)]
+        assert b[0] == 0 and b[-1] == 5000 and b == sorted(b)
+        assert max(costs) - min(costs) <= 2 * (np.diff(rp).max() + 6)
     # one giant row heavier than a share keeps bounds monotone
     rp2 = np.array([0, 1000, 1001, 1002, 1003], dtype=np.int64)
     b = partition.nnz_balanced_bounds(rp2, 4)
