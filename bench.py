@@ -6,7 +6,9 @@ on a seeded R-MAT graph shaped like ogbn-products (2,449,029 nodes,
 One step = one full forward over the whole graph: per layer the GCN
 aggregation (libgnnb200 SpMM), then X·W with bias and ReLU fused into the
 GEMM epilogue; with N GPUs the rows are split into N equal-nnz ranges (one
-process per GPU) and the layer-1 output rows are exchanged over NCCL.
+process per GPU; rows are dealt to ranks so that each gets the same number of
+rows and about the same cost) and the layer-1 output rows are exchanged between
+the GPUs over NVLink.
 
 Metric: algorithmic SpMM bytes of the step (CSR + gathered neighbour rows +
 output, per layer) divided by the step time, in GB/s, whole job. The JSON line
@@ -64,9 +66,14 @@ def parse_args():
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU-baseline sample time")
     ap.add_argument("--scale", type=float, default=1.0, help="scale the graph down (smoke runs only)")
-    ap.add_argument("--chunks", type=int, default=4, help="row pieces per rank, exchanged as they finish (N > 1)")
+    ap.add_argument("--chunks", type=int, default=1, help="row pieces per rank, exchanged as they finish (N > 1)")
     ap.add_argument("--exchange", choices=["push", "allgather"], default="push",
-                    help="N > 1: copy-engine pushes over IPC mappings, or NCCL all_gather on a padded layout")
+                    help="N > 1: pushes into the peers' IPC-mapped buffers, or NCCL all_gather")
+    ap.add_argument("--transport", choices=["sm", "ce"], default="sm",
+                    help="push transport: one SM kernel storing to every peer, or copy engines")
+    ap.add_argument("--push-ctas", type=int, default=0, help="grid of the SM push kernel (0: 4 per SM)")
+    ap.add_argument("--layout", choices=["balanced", "contiguous"], default="balanced",
+                    help="N > 1: rows dealt to ranks by cost, or contiguous cost-balanced ranges")
     return ap.parse_args()
 
 
@@ -110,8 +117,12 @@ class ClockSampler:
         try:
             self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                                          "-lms", "100", "-i", str(self.gpu)], stdout=self.file,
+                                          "-lms", "50", "-i", str(self.gpu)], stdout=self.file,
                                          stderr=subprocess.DEVNULL)
+            # the timed region starts only once sampling has (nvidia-smi takes a moment to start)
+            t0 = time.time()
+            while time.time() - t0 < 5.0 and os.path.getsize(self.file.name) == 0 and self.proc.poll() is None:
+                time.sleep(0.02)
         except Exception:
             self.proc = None
         return self
@@ -168,15 +179,16 @@ def build_problem(seed: int, device: torch.device, scale: float):
     return dict(n=n, nnz=int(ci.numel()), rp=rp, ci=ci, dis=dis, x=x, ws=ws, bs=bs)
 
 
-def describe(prob, world: int, gemm: str | None = None, chunks: int = 1, exchange: str = "push") -> dict:
+def describe(prob, world: int, gemm: str | None = None, chunks: int = 1, exchange: str = "push",
+             transport: str = "sm", layout: str = "balanced") -> dict:
     if gemm is None:
         gemm = "tcgen05-tf32" if N.lib().gnn_gemm_uses_tensor_cores(prob["n"], FEAT, FEAT) else "ffma-fp32"
     return {"workload": f"{WORKLOAD}: GCN {LAYERS} layers {FEAT}->{FEAT}->{FEAT}, ReLU between layers",
             "nodes": prob["n"], "csr_entries": int(prob["nnz"]), "feat_dim": FEAT, "layers": LAYERS,
             "self_loops": True, "graph": "R-MAT(0.57,0.19,0.19,0.05), symmetrised, de-duplicated",
             "parallelism": f"rows{world}" + ("" if world == 1 else
-                                             f"+ce_push_ipc_pieces{chunks}" if exchange == "push" else
-                                             f"+nccl_allgather_padded_pieces{chunks}"),
+                                             f"+{layout}_{transport}_push_pieces{chunks}" if exchange == "push" else
+                                             f"+{layout}_nccl_allgather_pieces{chunks}"),
             "l2": "inputs larger than L2 (X is %.2f GB), no flush" % (prob["n"] * FEAT * 4 / 1e9),
             "gemm": gemm}
 
@@ -195,25 +207,23 @@ def run_ours(args, rank: int, world: int, device: torch.device):
         shard = partition.make_shard(prob["rp"], prob["ci"], 0, n)
         bufs = {"agg": torch.empty(n, FEAT, device=device), "out0": torch.empty(n, FEAT, device=device),
                 "out1": torch.empty(n, FEAT, device=device)}
-    elif args.exchange == "push":
-        # equal-nnz row ranges cut into pieces; each piece's output is pushed to the peers as it finishes
-        bounds = partition.nnz_balanced_bounds(rp_cpu, world, partition.ROW_COST_IN_ENTRIES)
-        pieces = partition.make_pieces(prob["rp"], prob["ci"], bounds[rank], bounds[rank + 1], args.chunks)
-        shard = partition.PaddedShard(rank, pieces)  # used for its row / entry counts
-        del prob["rp"], prob["ci"]
-        torch.cuda.empty_cache()
-        exchange = partition.PeerRowExchange(n, FEAT, rank, world, device)
-        bufs = {"agg": torch.empty(max(p.num_rows for p in pieces), FEAT, device=device),
-                "out": torch.empty(shard.num_rows, FEAT, device=device)}
     else:
-        # padded chunk-major layout: each row piece's output is all-gathered while the next piece computes
-        layout = partition.make_padded_layout(rp_cpu, world, args.chunks)
+        # rows dealt to ranks by cost (or contiguous ranges), renumbered into the padded
+        # chunk-major exchange layout; sums are unchanged, only column ids are rewritten
+        layout = partition.make_padded_layout(rp_cpu, world, args.chunks, balanced=args.layout == "balanced",
+                                              row_cost=partition.ROW_COST_IN_ENTRIES)
         shard = partition.make_padded_shard(prob["rp"], prob["ci"], layout, rank)
         prob["dis"] = layout.pad_rows(prob["dis"])
         prob["x"] = layout.pad_rows(prob["x"])
         del prob["rp"], prob["ci"]
         torch.cuda.empty_cache()
-        bufs = partition.allgather_buffers(layout, FEAT, device)
+        if args.exchange == "push":
+            exchange = partition.PeerRowExchange(layout.padded_rows, FEAT, rank, world, device,
+                                                 transport=args.transport, ctas=args.push_ctas)
+            bufs = {"agg": torch.empty(layout.chunk_rows, FEAT, device=device),
+                    "out": torch.empty(layout.local_rows, FEAT, device=device)}
+        else:
+            bufs = partition.allgather_buffers(layout, FEAT, device)
     rows = shard.num_rows
     torch.backends.cuda.matmul.allow_tf32 = True  # the reference driver's --tf32 default
 
@@ -230,7 +240,7 @@ def run_ours(args, rank: int, world: int, device: torch.device):
                 x = out
             return x
         if args.exchange == "push":
-            return partition.gcn_forward_push(shard.pieces, prob["dis"], prob["x"], prob["ws"], prob["bs"], exchange,
+            return partition.gcn_forward_push(shard, prob["dis"], prob["x"], prob["ws"], prob["bs"], layout, exchange,
                                               bufs["agg"], bufs["out"], timers=timers)
         return partition.gcn_forward_allgather(shard, prob["dis"], prob["x"], prob["ws"], prob["bs"], layout, bufs,
                                                timers=timers)
@@ -320,7 +330,8 @@ def run_ours(args, rank: int, world: int, device: torch.device):
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
         "data": f"synthetic: seeded R-MAT graph (seed {args.seed}) with ogbn-products shape, N(0,1) features, "
                 "Glorot weights, zero bias",
-        "config": describe(prob, world, chunks=args.chunks, exchange=args.exchange),
+        "config": describe(prob, world, chunks=args.chunks, exchange=args.exchange, transport=args.transport,
+                           layout=args.layout),
         "roofline": {"bound": "hbm", "kernel": "spmm_vec_kernel + spmm_long_kernel (GCN aggregation)",
                      "achieved": round(achieved, 1) if achieved else None, "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4) if achieved else None, "peak_source": peak_kind,
@@ -436,7 +447,6 @@ def main() -> int:
         print(json.dumps(run_reference(args, device)), flush=True)
         return 0
     if world > 1:
-        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)
     try:
         res = run_ours(args, rank, world, device)

@@ -130,28 +130,47 @@ def gcn_forward_partitioned(shard: RowShard, deg_inv_sqrt: torch.Tensor, x_full:
 
 @dataclass
 class PaddedLayout:
-    """Chunk-major padded row layout for an all-gather exchange that can be pipelined.
+    """Where every global row lives in the padded [chunks*world*Mc, F] exchange matrix.
 
-    Every rank's local rows are cut into `chunks` pieces of `chunk_rows` (Mc)
-    rows; local row i of rank r lives at padded id
+    Rank r owns the rows order[r] (global ids, increasing) in that local order.
+    Its local rows are cut into `chunks` pieces of `chunk_rows` (Mc) rows, and
+    local row i of rank r lives at padded id
 
         (i // Mc) * world * Mc  +  r * Mc  +  (i % Mc)
 
     so piece c of every rank forms the contiguous block [c*world*Mc,
-    (c+1)*world*Mc) of the padded [chunks*world*Mc, F] matrix, and exchanging
-    piece c is one all_gather_into_tensor straight into the next layer's input
-    while piece c+1 is still being computed. Padding rows are never referenced
-    by any column id. The remap only rewrites column values; the CSR entry
-    order, and therefore every floating-point sum, is unchanged. With
-    chunks == 1 this is the plain layout r*Mc + i.
+    (c+1)*world*Mc) of the padded matrix: exchanging piece c is one
+    all_gather_into_tensor (or one push per peer) straight into the next
+    layer's input while piece c+1 is still being computed. Padding rows are
+    never referenced by any column id. The renumbering only rewrites column
+    values; CSR entry order, and therefore every floating-point sum, is
+    unchanged. With one rank's rows a contiguous range and chunks == 1 this is
+    the plain layout r*Mc + i.
     """
-    bounds: list[int]
+    order: list[torch.Tensor]
     chunk_rows: int
     chunks: int = 1
 
+    def __post_init__(self):
+        self.order = [torch.as_tensor(o, dtype=torch.int64).cpu().contiguous() for o in self.order]
+        n = sum(int(o.numel()) for o in self.order)
+        ids = torch.full((n,), -1, dtype=torch.int64)
+        mc, w = self.chunk_rows, self.world
+        for r, o in enumerate(self.order):
+            i = torch.arange(o.numel(), dtype=torch.int64)
+            ids[o] = (i // mc) * (w * mc) + r * mc + (i % mc)
+        if n and int(ids.min()) < 0:
+            raise ValueError("the rank orders must cover every row exactly once")
+        self.ids = ids
+        self._ids_on: dict = {}
+
     @property
     def world(self) -> int:
-        return len(self.bounds) - 1
+        return len(self.order)
+
+    @property
+    def num_nodes(self) -> int:
+        return int(self.ids.numel())
 
     @property
     def local_rows(self) -> int:
@@ -163,43 +182,73 @@ class PaddedLayout:
         return self.chunks * self.world * self.chunk_rows
 
     def rows_of(self, rank: int) -> int:
-        return self.bounds[rank + 1] - self.bounds[rank]
+        return int(self.order[rank].numel())
 
     def piece_range(self, rank: int, c: int) -> tuple[int, int]:
         """Local row range [lo, hi) of piece c on `rank` (possibly empty)."""
         lo = min(c * self.chunk_rows, self.rows_of(rank))
         return lo, min((c + 1) * self.chunk_rows, self.rows_of(rank))
 
+    def piece_first(self, rank: int, c: int) -> int:
+        """Padded id of piece c's first row on `rank`."""
+        return c * self.world * self.chunk_rows + rank * self.chunk_rows
+
+    def ids_on(self, device) -> torch.Tensor:
+        key = str(device)
+        if key not in self._ids_on:
+            self._ids_on[key] = self.ids.to(device)
+        return self._ids_on[key]
+
     def padded_ids(self, g: torch.Tensor) -> torch.Tensor:
-        b = torch.as_tensor(self.bounds, dtype=torch.int64, device=g.device)
-        g = g.to(torch.int64)
-        owner = torch.searchsorted(b[1:-1], g, right=True)
-        i = g - b[owner]
-        mc = self.chunk_rows
-        return (i // mc) * (self.world * mc) + owner * mc + (i % mc)
+        return self.ids_on(g.device)[g.to(torch.int64)]
 
     def pad_rows(self, full: torch.Tensor) -> torch.Tensor:
         """[N, ...] -> [padded_rows, ...] with zero padding rows."""
         out = torch.zeros((self.padded_rows,) + tuple(full.shape[1:]), dtype=full.dtype, device=full.device)
-        out[self.padded_ids(torch.arange(full.shape[0], device=full.device))] = full
+        out[self.ids_on(full.device)] = full
         return out
 
     def unpad_rows(self, padded: torch.Tensor) -> torch.Tensor:
-        return padded[self.padded_ids(torch.arange(self.bounds[-1], device=padded.device))]
+        return padded[self.ids_on(padded.device)]
 
 
-def make_padded_layout(row_ptr: np.ndarray, world: int, chunks: int = 1) -> PaddedLayout:
-    bounds = nnz_balanced_bounds(row_ptr, world)
-    max_rows = max(1, max(bounds[i + 1] - bounds[i] for i in range(world)))
+def balanced_row_order(row_ptr: np.ndarray, world: int, row_cost: float = ROW_COST_IN_ENTRIES) -> list[np.ndarray]:
+    """Deal rows to ranks so that every rank gets the same number of rows (+-1)
+    and about the same cost (entries + row_cost per row): rows sorted by cost,
+    heaviest first, are dealt 0, 1, .., W-1, W-1, .., 0, 0, 1, ... Each rank then
+    keeps its rows in increasing id order. Power-law hubs end up spread over all
+    ranks instead of packed into the first one, so neither the aggregation nor
+    the exchange (each rank sends its rows to every peer) is dominated by one rank."""
+    rp = np.asarray(row_ptr, dtype=np.int64)
+    n = rp.shape[0] - 1
+    cost = np.diff(rp).astype(np.float64) + float(row_cost)
+    by_cost = np.argsort(-cost, kind="stable")
+    p = np.arange(n)
+    w = p % world
+    owner = np.empty(n, dtype=np.int64)
+    owner[by_cost] = np.where((p // world) % 2 == 0, w, world - 1 - w)
+    return [np.nonzero(owner == r)[0] for r in range(world)]
+
+
+def make_padded_layout(row_ptr: np.ndarray, world: int, chunks: int = 1, *, balanced: bool = False,
+                       row_cost: float = 0.0) -> PaddedLayout:
+    """Contiguous cost-balanced row ranges (balanced=False), or rows dealt by
+    balanced_row_order (balanced=True), in `chunks` pieces per rank."""
+    if balanced:
+        order = balanced_row_order(row_ptr, world, row_cost)
+    else:
+        bounds = nnz_balanced_bounds(row_ptr, world, row_cost)
+        order = [np.arange(bounds[r], bounds[r + 1]) for r in range(world)]
+    max_rows = max(1, max(len(o) for o in order))
     chunks = max(1, min(int(chunks), max_rows))
-    return PaddedLayout(bounds, -(-max_rows // chunks), chunks)
+    return PaddedLayout(order, -(-max_rows // chunks), chunks)
 
 
 @dataclass
 class PaddedShard:
-    """One rank's rows as `chunks` row pieces with padded column ids."""
+    """One rank's rows as `chunks` row pieces with padded row and column ids."""
     rank: int
-    pieces: list[RowShard]  # piece c: row_begin = its first padded row, for the dis lookup
+    pieces: list[RowShard]  # piece c: row_begin = its first padded row (also the dis lookup)
 
     @property
     def num_rows(self) -> int:
@@ -211,15 +260,32 @@ class PaddedShard:
 
 
 def make_padded_shard(row_ptr: torch.Tensor, col_ind: torch.Tensor, layout: PaddedLayout, rank: int) -> PaddedShard:
-    """Rank `rank`'s rows cut into the layout's pieces, column ids rewritten to padded ids."""
-    b0 = layout.bounds[rank]
+    """Rank `rank`'s rows (layout.order[rank]) gathered into their own CSR, cut into
+    the layout's pieces, column ids rewritten to padded ids. Entry order within
+    every row is kept."""
+    dev = row_ptr.device
+    rows = layout.order[rank].to(dev)
+    rp64 = row_ptr.to(torch.int64)
+    starts = rp64[rows]
+    deg = rp64[rows + 1] - starts
+    local_rp = torch.zeros(rows.numel() + 1, dtype=torch.int64, device=dev)
+    torch.cumsum(deg, 0, out=local_rp[1:])
+    total = int(local_rp[-1])
+    first, last = (int(rows[0]), int(rows[-1])) if rows.numel() else (0, -1)
+    if rows.numel() and last - first + 1 == rows.numel():  # a contiguous range: a slice
+        e0 = int(rp64[first])
+        cols_g = col_ind[e0:e0 + total]
+    else:
+        entry = starts.repeat_interleave(deg) + (torch.arange(total, device=dev) - local_rp[:-1].repeat_interleave(deg))
+        cols_g = col_ind[entry]
+    cols = layout.padded_ids(cols_g).to(torch.int32) if total else col_ind[:0]
     pieces = []
     for c in range(layout.chunks):
         lo, hi = layout.piece_range(rank, c)
-        s = make_shard(row_ptr, col_ind, b0 + lo, b0 + hi)
-        cols = layout.padded_ids(s.col_ind).to(torch.int32).contiguous() if s.num_edges else s.col_ind
-        first = c * layout.world * layout.chunk_rows + rank * layout.chunk_rows
-        pieces.append(RowShard(first, first + (hi - lo), s.row_ptr, cols))
+        e0, e1 = int(local_rp[lo]), int(local_rp[hi])
+        rp_c = (local_rp[lo:hi + 1] - e0).to(row_ptr.dtype).contiguous()
+        head = layout.piece_first(rank, c)
+        pieces.append(RowShard(head, head + (hi - lo), rp_c, cols[e0:e1].contiguous()))
     return PaddedShard(rank, pieces)
 
 
@@ -304,24 +370,34 @@ class _PeerBlock:
 
 
 class PeerRowExchange:
-    """Copy-engine row exchange between the ranks of one node.
+    """Row exchange between the ranks of one node through IPC-mapped peer buffers.
 
-    Every rank holds two full [N, F] copies of "the next layer's input" in
-    memory it allocated itself (gnn_peer_alloc) and has mapped every peer's
-    copies through CUDA IPC. A layer writes its output rows straight into the
-    rank's own slice of the current copy; `push` sends a finished row range
-    to the same rows of every peer's current copy, one cudaMemcpyAsync per peer
-    on that peer's copy stream (copy engines over NVLink, no SM), ordered after
-    the producing kernel by an event. `finish` is the device-side barrier: a
-    one-element NCCL all_reduce issued after every push, which the compute
-    stream waits on before reading the copy. Copies alternate per exchange, so
-    a push never lands in a copy that a peer can still be reading: a rank
-    pushes into copy t only after the barrier of the previous exchange, which
-    every peer reaches only after its last read of copy t.
+    Every rank holds two [rows, F] copies of "the next layer's input" in memory
+    it allocated itself (gnn_peer_alloc) and has mapped every peer's copies
+    through CUDA IPC. A layer writes its output rows straight into the rank's
+    own rows of the current copy; `push` sends a finished row range to the same
+    rows of every peer's current copy once an event has fired:
+      * transport "sm": one gnn_peer_push kernel on the push stream reads the
+        rows once and stores them to all peers (SMs drive NVLink; `ctas` bounds
+        its grid so that it can share the GPU with the next piece's aggregation);
+      * transport "ce": one cudaMemcpyAsync per peer on that peer's stream
+        (copy engines, no SM).
+    `finish` is the device-side barrier: a one-element NCCL all_reduce issued
+    after every push, which the compute stream waits on before reading the copy.
+    Copies alternate per exchange, so a push never lands in a copy that a peer
+    can still be reading: a rank pushes into copy t only after the barrier of
+    the previous exchange, which every peer reaches only after its last read of
+    copy t.
     """
 
-    def __init__(self, num_rows: int, feat: int, rank: int, world: int, device: torch.device, group=None):
+    def __init__(self, num_rows: int, feat: int, rank: int, world: int, device: torch.device, group=None,
+                 transport: str = "sm", ctas: int = 0):
+        if transport not in ("sm", "ce"):
+            raise ValueError("transport must be 'sm' or 'ce'")
+        if world - 1 > 8 and transport == "sm":
+            raise ValueError("the sm transport pushes to at most 8 peers")
         self.rank, self.world, self.group = rank, world, group
+        self.transport, self.ctas = transport, int(ctas)
         self.device = device
         self.row_bytes = feat * 4
         self.shape = (num_rows, feat)
@@ -351,7 +427,10 @@ class PeerRowExchange:
                 buf = ctypes.create_string_buffer(everyone[p][t], hb)
                 N.call("gnn_ipc_open", buf, hb, dev, ctypes.byref(ptr))
                 self.peer_ptrs[t][p] = ptr.value
-        self.streams = {p: torch.cuda.Stream(device) for p in self.peer_ptrs[0]}
+        if transport == "ce":
+            self.streams = {p: torch.cuda.Stream(device) for p in self.peer_ptrs[0]}
+        else:
+            self.streams = {-1: torch.cuda.Stream(device)}
         self.barrier_stream = torch.cuda.Stream(device)
         self.flag = torch.zeros(1, device=device)
         self.turn = 0
@@ -362,11 +441,19 @@ class PeerRowExchange:
 
     def push(self, row_lo: int, row_hi: int, ready: torch.cuda.Event) -> None:
         """Send rows [row_lo, row_hi) of the current copy to every peer once `ready` has fired."""
-        if row_hi <= row_lo:
+        if row_hi <= row_lo or not self.peer_ptrs[self.turn]:
             return
         off = row_lo * self.row_bytes
         nbytes = (row_hi - row_lo) * self.row_bytes
         src = self.buffers[self.turn].data_ptr() + off
+        if self.transport == "sm":
+            s = self.streams[-1]
+            s.wait_event(ready)
+            dsts = [ptr + off for ptr in self.peer_ptrs[self.turn].values()]
+            arr = (ctypes.c_void_p * len(dsts))(*dsts)
+            N.call("gnn_peer_push", ctypes.c_void_p(src), arr, len(dsts), nbytes, self.ctas,
+                   ctypes.c_void_p(s.cuda_stream))
+            return
         for p, s in self.streams.items():
             s.wait_event(ready)
             N.call("gnn_copy_async", ctypes.c_void_p(self.peer_ptrs[self.turn][p] + off), ctypes.c_void_p(src),
@@ -398,39 +485,41 @@ class PeerRowExchange:
         self._blocks = []
 
 
-def gcn_forward_push(pieces: list[RowShard], deg_inv_sqrt: torch.Tensor, x_full: torch.Tensor,
-                     weights: list[torch.Tensor], biases: list[torch.Tensor], exchange: PeerRowExchange,
-                     agg: torch.Tensor, out: torch.Tensor, timers: dict | None = None) -> torch.Tensor:
-    """Multi-layer GCN over this rank's row pieces; layer outputs pushed to the peers piece by piece.
+def gcn_forward_push(shard: PaddedShard, dis_pad: torch.Tensor, x_pad: torch.Tensor, weights: list[torch.Tensor],
+                     biases: list[torch.Tensor], layout: PaddedLayout, exchange: PeerRowExchange, agg: torch.Tensor,
+                     out: torch.Tensor, timers: dict | None = None) -> torch.Tensor:
+    """Multi-layer GCN over a padded-layout shard; layer outputs pushed to the peers piece by piece.
 
-    pieces: this rank's rows as RowShards with global ids (make_pieces), in row
-    order. agg: [max piece rows, F] scratch. out: [rank rows, F] for the last
-    layer. Each piece's aggregation and X·W + b (+ReLU) land in the exchange's
-    current copy, whose rows then go to the peers while the next piece is computed.
+    exchange: a PeerRowExchange over layout.padded_rows rows. agg: [Mc, F]
+    scratch. out: [chunks*Mc, F] for the last layer (local order). Each piece's
+    aggregation and X·W + b (+ReLU) land in this rank's rows of the exchange's
+    current copy, which are then pushed to the peers while the next piece is
+    computed. Returns this rank's [rows, F] output rows (local order).
     """
     layers = len(weights)
-    first = pieces[0].row_begin
-    h = x_full
+    mc = layout.chunk_rows
+    h = x_pad
     for li in range(layers):
         last = li == layers - 1
-        dst = out if last else exchange.buffer()
-        base = first if last else 0
-        for piece in pieces:
+        for c, piece in enumerate(shard.pieces):
             if piece.num_rows == 0:
                 continue
             a = agg[:piece.num_rows]
             ev = _mark(timers, "spmm_begin")
-            spmm_gcn_shard(piece, deg_inv_sqrt, h, a)
+            spmm_gcn_shard(piece, dis_pad, h, a)
             _mark(timers, "spmm_end", ev)
-            native_ops.linear_forward_(a, weights[li], biases[li], dst[piece.row_begin - base:piece.row_end - base],
-                                       not last)
+            if last:
+                dst = out[c * mc:c * mc + piece.num_rows]
+            else:
+                dst = exchange.buffer()[piece.row_begin:piece.row_end]
+            native_ops.linear_forward_(a, weights[li], biases[li], dst, not last)
             if not last:
                 ready = torch.cuda.Event()
                 ready.record()
                 exchange.push(piece.row_begin, piece.row_end, ready)
         if not last:
             h = exchange.finish()
-    return out
+    return out[:shard.num_rows]
 
 
 def _mark(timers: dict | None, key: str, begin=None):

@@ -1,9 +1,10 @@
 """Row-partitioned multi-GPU GCN forward equals the single-GPU forward bit for bit.
 
-Covers the three exchanges: NCCL broadcast, NCCL all_gather on the padded
-chunk-major layout (1 and 3 pieces), and copy-engine pushes into the peers'
-IPC-mapped buffers (1 and 3 pieces, three steps in a row so both of the
-alternating buffers are used).
+Covers the three exchanges: NCCL broadcast; NCCL all_gather on the padded
+chunk-major layout; pushes into the peers' IPC-mapped buffers by the SM push
+kernel and by copy engines (three steps in a row, so both alternating buffers
+are used) — on contiguous row ranges and on rows dealt to ranks by cost, with
+1 to 3 pieces per rank.
 
 Runs only where at least two GPUs are visible (spawned ranks, one GPU each,
 NCCL with NVLS off). The long-row threshold is fixed so every rank uses the
@@ -61,34 +62,34 @@ def _worker(rank, world, port, q):
         out = partition.gcn_forward_partitioned(shard, dis, x, ws, bs, bounds, rank, bufs)
         full = torch.empty(N_NODES, FEAT, device=dev)
         partition.exchange_rows(out, full, bounds, rank)
-        # padded chunk-major layout, pipelined all_gather per row piece
+        # padded chunk-major layouts (contiguous ranges or rows dealt by cost), both exchanges
         padded = []
-        for chunks in (1, 3):
-            lay = partition.make_padded_layout(rp.cpu().numpy(), world, chunks)
+        rp_np = rp.cpu().numpy()
+        cases = [("allgather", None, 1, False), ("allgather", None, 3, True),
+                 ("push", "sm", 1, True), ("push", "ce", 3, True), ("push", "sm", 2, False)]
+        for how, transport, chunks, balanced in cases:
+            lay = partition.make_padded_layout(rp_np, world, chunks, balanced=balanced, row_cost=6)
             pshard = partition.make_padded_shard(rp, ci, lay, rank)
-            pbufs = partition.allgather_buffers(lay, FEAT, dev)
-            pout = partition.gcn_forward_allgather(pshard, lay.pad_rows(dis), lay.pad_rows(x), ws, bs, lay, pbufs)
+            dis_p, x_p = lay.pad_rows(dis), lay.pad_rows(x)
+            if how == "allgather":
+                pbufs = partition.allgather_buffers(lay, FEAT, dev)
+                pout = partition.gcn_forward_allgather(pshard, dis_p, x_p, ws, bs, lay, pbufs)
+            else:
+                ex = partition.PeerRowExchange(lay.padded_rows, FEAT, rank, world, dev, transport=transport)
+                agg = torch.empty(lay.chunk_rows, FEAT, device=dev)
+                mine = torch.empty(lay.local_rows, FEAT, device=dev)
+                for _ in range(3):  # repeated steps alternate the two copies
+                    pout = partition.gcn_forward_push(pshard, dis_p, x_p, ws, bs, lay, ex, agg, mine)
             # collect the final rows through the same layout
             pfull = torch.zeros(lay.local_rows, FEAT, device=dev)
             pfull[:pshard.num_rows] = pout
             gathered = torch.empty(lay.padded_rows, FEAT, device=dev)
+            mc = lay.chunk_rows
             for c in range(lay.chunks):
-                mc = lay.chunk_rows
                 dist.all_gather_into_tensor(gathered[c * world * mc:(c + 1) * world * mc], pfull[c * mc:(c + 1) * mc])
             padded.append(lay.unpad_rows(gathered).cpu().numpy())
-        # copy-engine pushes over IPC mappings, pieces of equal nnz
-        for chunks in (1, 3):
-            pieces = partition.make_pieces(rp, ci, bounds[rank], bounds[rank + 1], chunks)
-            ex = partition.PeerRowExchange(N_NODES, FEAT, rank, world, dev)
-            agg = torch.empty(max(p.num_rows for p in pieces), FEAT, device=dev)
-            mine = torch.empty(rows, FEAT, device=dev)
-            for _ in range(3):  # repeated steps alternate the two copies
-                partition.gcn_forward_push(pieces, dis, x, ws, bs, ex, agg, mine)
-            full_p = torch.empty(N_NODES, FEAT, device=dev)
-            partition.exchange_rows(mine, full_p, bounds, rank)
-            torch.cuda.synchronize(dev)
-            padded.append(full_p.cpu().numpy())
-            ex.close()
+            if how == "push":
+                ex.close()
         torch.cuda.synchronize(dev)
         q.put((rank, full.cpu().numpy(), padded))
     finally:

@@ -97,38 +97,67 @@ def test_piece_bounds_and_pieces():
 def test_padded_layout_maps():
     rp = np.array([0, 3, 3, 10, 12, 20, 21, 30], dtype=np.int64)  # 7 rows
     lay = partition.make_padded_layout(rp, 3)
-    assert lay.bounds[0] == 0 and lay.bounds[-1] == 7 and lay.world == 3
+    assert lay.world == 3 and lay.num_nodes == 7
+    assert [int(o[0]) for o in lay.order if o.numel()] == sorted(int(o[0]) for o in lay.order if o.numel())
     g = torch.arange(7)
     p = lay.padded_ids(g)
-    assert torch.all(p[1:] > p[:-1])  # one piece: the plain r*Mc + i layout, increasing
+    assert torch.all(p[1:] > p[:-1])  # contiguous ranges, one piece: the plain r*Mc + i layout, increasing
     x = torch.arange(7 * 2, dtype=torch.float32).view(7, 2)
     xp = lay.pad_rows(x)
     assert xp.shape == (lay.padded_rows, 2)
     assert torch.equal(xp[p], x) and torch.equal(lay.unpad_rows(xp), x)
 
 
-@pytest.mark.parametrize("world,chunks", [(2, 3), (3, 2), (4, 5), (2, 64)])
-def test_padded_layout_chunk_major(world, chunks):
+@pytest.mark.parametrize("world", [2, 3, 8])
+def test_balanced_row_order(world):
+    u, v = synth.rmat_undirected(4000, 40000, seed=world)
+    s, d = synth.symmetrize(u, v)
+    from gnn_cuda_b200.GNN_cuda_common import graph_utils as G
+    rp = G.build_gcn_normalized_csr(s, d, num_nodes=4000).row_ptr.numpy().astype(np.int64)
+    order = partition.balanced_row_order(rp, world, row_cost=6)
+    allrows = np.sort(np.concatenate(order))
+    assert np.array_equal(allrows, np.arange(4000))  # every row exactly once
+    sizes = [len(o) for o in order]
+    assert max(sizes) - min(sizes) <= 1  # equal rows per rank
+    deg = np.diff(rp)
+    costs = [float((deg[o] + 6).sum()) for o in order]
+    assert max(costs) - min(costs) <= deg.max() + 6  # the snake deal keeps costs within one row
+    assert all(np.all(np.diff(o) > 0) for o in order)  # increasing ids within a rank
+
+
+@pytest.mark.parametrize("world,chunks,balanced", [(2, 3, False), (3, 2, False), (4, 5, True), (2, 64, True),
+                                                   (3, 1, True)])
+def test_padded_layout_chunk_major(world, chunks, balanced):
     u, v = synth.rmat_undirected(300, 2000, seed=world + chunks)
     s, d = synth.symmetrize(u, v)
     from gnn_cuda_b200.GNN_cuda_common import graph_utils as G
     g = G.build_gcn_normalized_csr(s, d, num_nodes=300)
-    lay = partition.make_padded_layout(g.row_ptr.numpy(), world, chunks)
+    lay = partition.make_padded_layout(g.row_ptr.numpy(), world, chunks, balanced=balanced, row_cost=6)
     ids = lay.padded_ids(torch.arange(300))
     assert len(set(ids.tolist())) == 300 and int(ids.max()) < lay.padded_rows  # injective, in range
     mc = lay.chunk_rows
     for r in range(world):
+        rows = lay.order[r]
         for c in range(lay.chunks):
             lo, hi = lay.piece_range(r, c)
-            got = ids[lay.bounds[r] + lo:lay.bounds[r] + hi]
-            want = c * world * mc + r * mc + torch.arange(hi - lo)
+            got = ids[rows[lo:hi]]
+            want = lay.piece_first(r, c) + torch.arange(hi - lo)
             assert torch.equal(got, want)  # piece c of rank r is one contiguous block
-    # the pieces' rows and entries add up to the shard
-    sh = partition.make_padded_shard(g.row_ptr, g.col_ind, lay, 1)
-    b0, b1 = lay.bounds[1], lay.bounds[2]
-    assert sh.num_rows == b1 - b0 and sh.num_edges == int(g.row_ptr[b1] - g.row_ptr[b0])
-    cols = torch.cat([p.col_ind.to(torch.int64) for p in sh.pieces])
-    assert torch.equal(cols, ids[g.col_ind[g.row_ptr[b0]:g.row_ptr[b1]].to(torch.int64)])
+    # the shard holds exactly its rows' entries, in CSR order, renumbered
+    rp = g.row_ptr.to(torch.int64)
+    for r in range(world):
+        sh = partition.make_padded_shard(g.row_ptr, g.col_ind, lay, r)
+        rows = lay.order[r]
+        want_cols = torch.cat([g.col_ind[rp[v]:rp[v + 1]] for v in rows.tolist()] or [g.col_ind[:0]])
+        assert sh.num_rows == rows.numel() and sh.num_edges == want_cols.numel()
+        cols = torch.cat([p.col_ind.to(torch.int64) for p in sh.pieces])
+        assert torch.equal(cols, ids[want_cols.to(torch.int64)])
+        for c, p in enumerate(sh.pieces):
+            lo, hi = lay.piece_range(r, c)
+            assert p.row_begin == lay.piece_first(r, c) and p.num_rows == hi - lo
+            seg = rows[lo:hi]
+            assert int(p.row_ptr[0]) == 0
+            assert torch.equal(torch.diff(p.row_ptr.to(torch.int64)), rp[seg + 1] - rp[seg])  # row degrees
     x = torch.randn(300, 3)
     assert torch.equal(lay.unpad_rows(lay.pad_rows(x)), x)
 
@@ -145,8 +174,8 @@ def _worker_padded(rank, world, port, q):
         g = G.build_gcn_normalized_csr(s, d, num_nodes=n)
         x = synth.features(n, f, seed=8)
         results = []
-        for chunks in (1, 4):
-            lay = partition.make_padded_layout(g.row_ptr.numpy(), world, chunks)
+        for chunks, balanced in ((1, False), (4, False), (1, True), (3, True)):
+            lay = partition.make_padded_layout(g.row_ptr.numpy(), world, chunks, balanced=balanced, row_cost=6)
             shard = partition.make_padded_shard(g.row_ptr, g.col_ind, lay, rank)
             dis_pad = lay.pad_rows(g.deg_inv_sqrt).numpy()
             x_pad = lay.pad_rows(x).numpy()
