@@ -75,6 +75,9 @@ def parse_args():
     ap.add_argument("--push-ctas", type=int, default=0, help="grid of the SM push kernel (0: 4 per SM)")
     ap.add_argument("--layout", choices=["balanced", "contiguous"], default="balanced",
                     help="N > 1: rows dealt to ranks by cost, or contiguous cost-balanced ranges")
+    ap.add_argument("--workload", choices=["gcn_products_like", "locality_products_like"],
+                    default="gcn_products_like",
+                    help="the GCN forward (default), or the UVM locality preprocessing of the same graph (1 GPU)")
     return ap.parse_args()
 
 
@@ -436,6 +439,80 @@ def run_reference(args, device: torch.device):
             "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+# ---------------------------------------------------------------------------
+# locality preprocessing workload (the input of spmm_mode=optimized)
+# ---------------------------------------------------------------------------
+
+LOCALITY_METRIC = "GCN locality preprocessing throughput (CSR entries/s), 1 B200"
+LOCALITY_CPU_SCALE = 1.0 / 16
+
+
+def _locality_graph(seed: int, device, scale: float):
+    src, dst, n = synth.make_graph(WORKLOAD, seed=seed, device=device, scale_nodes=scale)
+    return src, dst, n
+
+
+def run_locality(args, device: torch.device) -> dict:
+    from gnn_cuda_b200.GNN_cuda_common.locality import preprocess_gcn_graph
+    src, dst, n = _locality_graph(args.seed, device, args.scale)
+    entries = int(src.numel()) + n  # CSR entries incl. self-loops (the graph is duplicate-free)
+    for _ in range(max(1, args.warmup)):
+        preprocess_gcn_graph(src, dst, num_nodes=n)
+    torch.cuda.synchronize(device)
+    launches0 = N.lib().gnn_kernel_launches()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device.index) as clocks:
+        t0.record()
+        for _ in range(args.steps):
+            pay = preprocess_gcn_graph(src, dst, num_nodes=n)
+        t1.record()
+        torch.cuda.synchronize(device)
+    ms = t0.elapsed_time(t1) / args.steps
+    launches = N.lib().gnn_kernel_launches() - launches0
+    value = entries / (ms * 1e-3) / 1e6
+    # e2e: host edge lists in, the payload back on the host
+    h_src, h_dst = src.cpu().pin_memory(), dst.cpu().pin_memory()
+    e0 = time.perf_counter()
+    pay_h = preprocess_gcn_graph(h_src, h_dst, num_nodes=n)
+    e2e_s = time.perf_counter() - e0
+    d2h = sum(v.numel() * v.element_size() for v in pay_h.values() if isinstance(v, torch.Tensor))
+    res = {
+        "metric": LOCALITY_METRIC, "value": round(value, 2), "unit": "M entries/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "int64",
+        "data": f"synthetic: seeded R-MAT graph (seed {args.seed}) with ogbn-products shape",
+        "config": {"workload": "locality_products_like: page schedule -> co-access order -> hot partition -> "
+                               "renumbered page schedule (run/preprocess_gcn_graph.py defaults)",
+                   "nodes": n, "csr_entries": entries, "feat_dim": 128, "page_bytes": 4096,
+                   "hot_cutoff": int(pay["hot_node_cutoff"]), "num_pages": int(pay["num_pages"])},
+        "e2e": {"value": round(entries / e2e_s / 1e6, 2), "unit": "M entries/s",
+                "h2d_bytes_per_step": int(2 * src.numel() * 8), "d2h_bytes_per_step": int(d2h),
+                "api": "gnn_cuda_b200.GNN_cuda_common.locality.preprocess_gcn_graph on host tensors"},
+        "gpu_launches": int(launches), "clocks": clocks.summary(),
+    }
+    if args.cpu_seconds > 0:
+        res["cpu_baseline"] = locality_cpu_baseline(args.seed)
+    return res
+
+
+def locality_cpu_baseline(seed: int) -> dict:
+    """The numpy restatement of the reference's preprocessing (oracle/locality.py,
+    one core) on the same generator at 1/16 of the nodes and entries. The
+    reference's own functions need a dense [row blocks x pages] int64 array
+    (94 GB at the full products shape), so the port stands in for them."""
+    from oracle import locality as OL
+    src, dst, n = _locality_graph(seed, "cpu", LOCALITY_CPU_SCALE)
+    s, d = src.numpy(), dst.numpy()
+    t0 = time.perf_counter()
+    OL.preprocess(s, d, num_nodes=n)
+    dt = time.perf_counter() - t0
+    entries = int(s.size) + n
+    return {"value": round(entries / dt / 1e6, 3), "unit": "M entries/s", "cores": 1, "kind": "port",
+            "sample": f"the whole preprocessing chain on a 1/16-scale graph ({n} nodes, {entries} entries) "
+                      f"in {dt:.2f} s; vectorised numpy restatement of graph_utils.py:174-446"}
+
+
 def main() -> int:
     args = parse_args()
     rank = int(os.environ.get("RANK", "0"))
@@ -445,6 +522,18 @@ def main() -> int:
         log(f"[bench] WORLD_SIZE={world} but --gpus={args.gpus}; using WORLD_SIZE")
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
+    if args.workload == "locality_products_like":
+        if rank != 0:
+            return 0
+        if args.impl == "reference":
+            cpu = locality_cpu_baseline(args.seed)
+            print(json.dumps({"metric": LOCALITY_METRIC, "value": cpu["value"], "unit": cpu["unit"], "n_gpus": 1,
+                              "impl": "reference", "higher_is_better": True, "cpu_baseline": cpu,
+                              "e2e": {"value": cpu["value"], "unit": cpu["unit"], "h2d_bytes_per_step": 0,
+                                      "d2h_bytes_per_step": 0}}), flush=True)
+        else:
+            print(json.dumps(run_locality(args, device)), flush=True)
+        return 0
     if args.impl == "reference":
         if rank != 0:
             return 0

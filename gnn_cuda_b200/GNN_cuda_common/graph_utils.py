@@ -265,3 +265,11 @@ def resolve_dataset_path(dataset: str, *, data_root: str) -> str:
     if "/" in dataset or "\\" in dataset or dataset.endswith(".npz"):
         raise ValueError("--dataset only accepts a dataset name or 'all'")
     return str(Path(data_root) / f"{dataset}.npz")
+
+
+# UVM locality preprocessing (graph_utils.py:174-446 of the reference), computed on the GPU.
+from .locality import (  # noqa: E402,F401  (re-exported under the reference's module)
+    build_coaccess_feature_permutation,
+    build_hot_partition_feature_permutation,
+    build_page_reuse_schedule_metadata,
+)

@@ -82,6 +82,18 @@ PROTOTYPES: dict[str, tuple[object, list[object]]] = {
                              ctypes.POINTER(_i64), _vp, _sz, _vp]),
     "gnn_csr_deg_inv_sqrt": (_i32, [_vp, _i32, _i64, _vp, _i64, _vp, _vp]),
     "gnn_csr_edge_weight": (_i32, [_vp, _i32, _vp, _vp, _i64, _vp, _vp]),
+    "gnn_locality_workspace_bytes": (_sz, [_i64, _i64, _i64]),
+    "gnn_locality_page_schedule": (
+        _i32, [_vp, _i32, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp,
+               ctypes.POINTER(_i64), ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double), _vp, _sz, _vp]),
+    "gnn_locality_count_histogram": (_i32, [_vp, _i64, _vp, _i64, _vp]),
+    "gnn_locality_coaccess_permutation": (
+        _i32, [_vp, _i32, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _sz, _vp]),
+    "gnn_locality_hot_partition": (
+        _i32, [_vp, _i64, _i64, _i32, _vp, ctypes.c_double, ctypes.c_double, _i64, _vp, _vp, _vp, _vp,
+               ctypes.POINTER(_i64), ctypes.POINTER(_i64), ctypes.POINTER(_i64), ctypes.POINTER(_i64), _vp, _sz,
+               _vp]),
+    "gnn_permute_edges": (_i32, [_vp, _vp, _i64, _vp, _i64, _vp, _vp, _vp, _sz, _vp]),
     "gnn_peer_alloc": (_i32, [_sz, _i32, ctypes.POINTER(_vp)]),
     "gnn_peer_free": (_i32, [_vp, _i32]),
     "gnn_ipc_handle_bytes": (_sz, []),

@@ -311,6 +311,79 @@ int gnn_csr_deg_inv_sqrt(const void* row_ptr, int row_ptr_type, int64_t num_node
 int gnn_csr_edge_weight(const void* row_ptr, int row_ptr_type, const int32_t* col_ind, const float* deg_inv_sqrt,
                         int64_t num_nodes, float* edge_weight, gnn_stream_t stream);
 
+/* ---- UVM locality preprocessing on the device ------------------------------
+ * Replaces the host preprocessing behind spmm_mode="optimized":
+ * build_page_reuse_schedule_metadata (GNN_cuda_common/graph_utils.py:244-372),
+ * build_coaccess_feature_permutation (:375-446),
+ * build_hot_partition_feature_permutation (:174-241) and
+ * apply_graph_permutation (:76-85), as chained by run/preprocess_gcn_graph.py:40-120.
+ * Same arrays bit for bit (integer orders with the reference's tie-breaks);
+ * the float64 ratios are formed on the host from integer totals exactly as
+ * numpy forms them. The CSR inputs are the dst-major CSR with self-loops that
+ * gnn_csr_build produces (graph_utils.py:258-267 builds the same one). These
+ * calls validate their index inputs on the device (a bad id is an error, never
+ * an out-of-bounds access), read host scalars back, and so synchronise `stream`.
+ * All int64 outputs are device arrays the caller allocates. */
+
+/* Scratch for every gnn_locality_* call on a graph of num_nodes nodes and
+ * num_entries CSR entries with top-k lists up to max_k (the larger of
+ * signature_topk and window_cache_pages; <= 4096). Queries the current device;
+ * 0 on failure. */
+size_t gnn_locality_workspace_bytes(int64_t num_nodes, int64_t num_entries, int64_t max_k);
+
+/* Page metadata and row schedule of a CSR (build_page_reuse_schedule_metadata).
+ * With P = ceil(num_nodes / rows_per_page), NB = ceil(num_nodes / row_block_size),
+ * NW = ceil(num_nodes / (row_block_size * window_num_blocks)), k = signature_topk:
+ * page_histogram [P], hot_pages [min(hot_cache_pages, P)], row_schedule
+ * [num_nodes], block_hot_pages [NB, k], window_hot_pages [NW, window_cache_pages]
+ * (pages padded with P); host outputs: the largest page count (the length - 1
+ * of page_reuse_histogram, see gnn_locality_count_histogram), hot_coverage and
+ * avg_window_hot_coverage. num_entries < 2^32. */
+int gnn_locality_page_schedule(const void* row_ptr, int row_ptr_type, const int32_t* col_ind, int64_t num_nodes,
+                               int64_t num_entries, int64_t rows_per_page, int64_t row_block_size,
+                               int64_t window_num_blocks, int64_t window_cache_pages, int64_t hot_cache_pages,
+                               int64_t signature_topk, int64_t* page_histogram, int64_t* hot_pages,
+                               int64_t* row_schedule, int64_t* block_hot_pages, int64_t* window_hot_pages,
+                               int64_t* max_page_count, double* hot_coverage, double* avg_window_hot_coverage,
+                               void* workspace, size_t workspace_bytes, gnn_stream_t stream);
+
+/* hist[v] = number of i with values[i] == v for 1 <= v < hist_len, hist[0] = 0:
+ * np.bincount of the non-zero values (graph_utils.py:273-278, the page reuse
+ * histogram, with hist_len = largest page count + 1). */
+int gnn_locality_count_histogram(const int64_t* values, int64_t count, int64_t* hist, int64_t hist_len,
+                                 gnn_stream_t stream);
+
+/* Node order by co-access windows (build_coaccess_feature_permutation):
+ * perm, inv_perm [num_nodes]. row_schedule must be a permutation of
+ * [0, num_nodes); rows_per_window = row_block_size * window_num_blocks. */
+int gnn_locality_coaccess_permutation(const void* row_ptr, int row_ptr_type, const int32_t* col_ind,
+                                      int64_t num_nodes, int64_t num_entries, const int64_t* row_schedule,
+                                      int64_t rows_per_window, int64_t signature_topk, int64_t* perm,
+                                      int64_t* inv_perm, void* workspace, size_t workspace_bytes,
+                                      gnn_stream_t stream);
+
+/* Hot prefix / cold suffix order (build_hot_partition_feature_permutation).
+ * src: the int64 source id of every edge (plus one access per node when
+ * add_self_loops). Outputs: access_count [num_nodes], sorted_nodes [num_nodes]
+ * (stable descending order of access_count; hot_nodes is its first
+ * *hot_node_cutoff entries), perm and inv_perm [num_nodes]; host: the cutoff,
+ * the hot_min_nodes actually used, total and hot access counts. base_order
+ * (NULL for none) must be a permutation of [0, num_nodes) — the reference only
+ * checks its length. */
+int gnn_locality_hot_partition(const int64_t* src, int64_t num_entries, int64_t num_nodes, int add_self_loops,
+                               const int64_t* base_order, double hot_access_coverage, double hot_max_ratio,
+                               int64_t hot_min_nodes, int64_t* access_count, int64_t* sorted_nodes, int64_t* perm,
+                               int64_t* inv_perm, int64_t* hot_node_cutoff, int64_t* min_nodes_used,
+                               int64_t* total_access, int64_t* hot_access, void* workspace,
+                               size_t workspace_bytes, gnn_stream_t stream);
+
+/* src_out[i] = inv_perm[src[i]], dst_out[i] = inv_perm[dst[i]]
+ * (apply_graph_permutation, graph_utils.py:76-85). workspace: >= 256 bytes of
+ * device memory for the error flag. */
+int gnn_permute_edges(const int64_t* src, const int64_t* dst, int64_t num_entries, const int64_t* inv_perm,
+                      int64_t num_nodes, int64_t* src_out, int64_t* dst_out, void* workspace, size_t workspace_bytes,
+                      gnn_stream_t stream);
+
 /* ---- peer memory for the row-partitioned multi-GPU mode -------------------- *
  * No counterpart in the reference, which runs on one GPU. A rank allocates its
  * copy of the next layer's input with gnn_peer_alloc, exports it with

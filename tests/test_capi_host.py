@@ -103,3 +103,25 @@ def test_allocator_modes():
     assert A.prefers_hmm_spmm("device", "hmm") and not A.prefers_hmm_spmm("uvm", "device")
     with pytest.raises(ValueError, match="requires a CUDA device"):
         A.managed_empty((2, 2), dtype=torch.float32, device=torch.device("cpu"))
+
+
+def test_locality_arguments_rejected_without_device():
+    L = N.lib()
+    page = L.gnn_locality_page_schedule
+    # num_nodes must be >= 1; top-k lists bounded; required outputs non-NULL
+    rc = page(None, 0, None, 0, 0, 8, 64, 4, 8, 16, 4, None, None, None, None, None, None, None, None, None, 0, None)
+    assert rc == 1 and "num_nodes" in N.last_error()
+    rc = page(None, 0, None, 10, 0, 8, 64, 4, 8, 16, 0, None, None, None, None, None, None, None, None, None, 0, None)
+    assert rc == 1 and "signature_topk" in N.last_error()
+    rc = page(None, 0, None, 10, 0, 8, 64, 4, 8, 16, 4, None, None, None, None, None, None, None, None, None, 0, None)
+    assert rc == 2 and "NULL" in N.last_error()
+    rc = L.gnn_locality_coaccess_permutation(None, 0, None, 10, 1 << 33, None, 256, 4, None, None, None, 0, None)
+    assert rc == 1 and "num_entries" in N.last_error()
+    cut = [ctypes.c_int64(0) for _ in range(4)]
+    rc = L.gnn_locality_hot_partition(None, 0, 0, 1, None, 0.8, 0.25, 256, None, None, None, None,
+                                      *[ctypes.byref(c) for c in cut], None, 0, None)
+    assert rc == 1 and "num_nodes" in N.last_error()
+    assert L.gnn_locality_workspace_bytes(10, 10, 5000) == 0
+    assert L.gnn_locality_count_histogram(None, 0, None, 0, None) == 1
+    assert L.gnn_permute_edges(None, None, 0, None, 5, None, None, None, 0, None) == 0
+    assert L.gnn_permute_edges(None, None, 4, None, 5, None, None, None, 0, None) == 2
