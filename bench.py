@@ -68,8 +68,9 @@ def parse_args():
     ap.add_argument("--scale", type=float, default=1.0, help="scale the graph down (smoke runs only)")
     ap.add_argument("--chunks", type=int, default=0,
                     help="row pieces per rank, exchanged as they finish (N > 1; 0: 2 from 8 GPUs up, else 1)")
-    ap.add_argument("--exchange", choices=["push", "allgather"], default="push",
-                    help="N > 1: pushes into the peers' IPC-mapped buffers, or NCCL all_gather")
+    ap.add_argument("--exchange", choices=["push", "halo", "allgather"], default="push",
+                    help="N > 1: pushes of whole row pieces into the peers' IPC-mapped buffers, pushes of only "
+                         "the rows each peer reads (halo), or NCCL all_gather")
     ap.add_argument("--transport", choices=["sm", "ce"], default="sm",
                     help="push transport: one SM kernel storing to every peer, or copy engines")
     ap.add_argument("--push-ctas", type=int, default=0, help="grid of the SM push kernel (0: 4 per SM)")
@@ -192,6 +193,7 @@ def describe(prob, world: int, gemm: str | None = None, chunks: int = 1, exchang
             "self_loops": True, "graph": "R-MAT(0.57,0.19,0.19,0.05), symmetrised, de-duplicated",
             "parallelism": f"rows{world}" + ("" if world == 1 else
                                              f"+{layout}_{transport}_push_pieces{chunks}" if exchange == "push" else
+                                             f"+{layout}_halo_push_pieces{chunks}" if exchange == "halo" else
                                              f"+{layout}_nccl_allgather_pieces{chunks}"),
             "l2": "inputs larger than L2 (X is %.2f GB), no flush" % (prob["n"] * FEAT * 4 / 1e9),
             "gemm": gemm}
@@ -207,6 +209,7 @@ def run_ours(args, rank: int, world: int, device: torch.device):
     nnz = int(prob["ci"].numel())
     rp_cpu = prob["rp"].to(torch.int64).cpu().numpy()
     exchange = None
+    halo = None
     if args.chunks <= 0:
         # measured on B200: two pieces hide part of the exchange at 8 GPUs (3.42 vs 3.69 ms per step)
         args.chunks = 2 if world >= 8 else 1
@@ -220,13 +223,16 @@ def run_ours(args, rank: int, world: int, device: torch.device):
         layout = partition.make_padded_layout(rp_cpu, world, args.chunks, balanced=args.layout == "balanced",
                                               row_cost=partition.ROW_COST_IN_ENTRIES)
         shard = partition.make_padded_shard(prob["rp"], prob["ci"], layout, rank)
+        if args.exchange == "halo":
+            halo = partition.make_halo_plan(prob["rp"], prob["ci"], layout, rank)
         prob["dis"] = layout.pad_rows(prob["dis"])
         prob["x"] = layout.pad_rows(prob["x"])
         del prob["rp"], prob["ci"]
         torch.cuda.empty_cache()
-        if args.exchange == "push":
+        if args.exchange in ("push", "halo"):
             exchange = partition.PeerRowExchange(layout.padded_rows, FEAT, rank, world, device,
-                                                 transport=args.transport, ctas=args.push_ctas)
+                                                 transport="sm" if args.exchange == "halo" else args.transport,
+                                                 ctas=args.push_ctas)
             bufs = {"agg": torch.empty(layout.chunk_rows, FEAT, device=device),
                     "out": torch.empty(layout.local_rows, FEAT, device=device)}
         else:
@@ -246,9 +252,9 @@ def run_ours(args, rank: int, world: int, device: torch.device):
                 agg_ops.linear_forward_(bufs["agg"], prob["ws"][li], prob["bs"][li], out, li != LAYERS - 1)
                 x = out
             return x
-        if args.exchange == "push":
+        if args.exchange in ("push", "halo"):
             return partition.gcn_forward_push(shard, prob["dis"], prob["x"], prob["ws"], prob["bs"], layout, exchange,
-                                              bufs["agg"], bufs["out"], timers=timers)
+                                              bufs["agg"], bufs["out"], timers=timers, halo=halo)
         return partition.gcn_forward_allgather(shard, prob["dis"], prob["x"], prob["ws"], prob["bs"], layout, bufs,
                                                timers=timers)
 

@@ -103,6 +103,7 @@ PROTOTYPES: dict[str, tuple[object, list[object]]] = {
     "gnn_can_access_peer": (_i32, [_i32, _i32, ctypes.POINTER(_i32)]),
     "gnn_copy_async": (_i32, [_vp, _vp, _sz, _vp]),
     "gnn_peer_push": (_i32, [_vp, ctypes.POINTER(_vp), _i32, _sz, _i32, _vp]),
+    "gnn_peer_push_rows": (_i32, [_vp, ctypes.POINTER(_vp), _i32, _vp, ctypes.POINTER(_i64), _i64, _i64, _i32, _vp]),
 }
 
 

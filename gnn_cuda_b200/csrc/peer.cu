@@ -167,3 +167,79 @@ extern "C" int gnn_peer_push(const void* src, void* const* dsts, int ndst, size_
   clear_error();
   return GNN_OK;
 }
+
+namespace {
+
+struct ListedTargets {
+  char* dst[kMaxPeers];
+  int64_t off[kMaxPeers + 1];  // rows [off[q], off[q+1]) of the id list go to dst[q]
+};
+
+// One warp per listed row: copies row `ids[w]` (row_bytes, 16-byte words) from
+// src to the same row of the destination that owns list entry w. Every
+// destination shares src's row layout, so the row offset is the same on both
+// sides. Ids outside [0, max_rows) are skipped (the host validated them).
+__global__ void __launch_bounds__(512) push_listed_rows_kernel(const char* __restrict__ src, ListedTargets t,
+                                                               int ntargets, const int32_t* __restrict__ ids,
+                                                               int64_t row_words, int64_t max_rows) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  const int64_t total = t.off[ntargets];
+  for (int64_t w = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); w < total;
+       w += warps) {
+    int q = 0;
+#pragma unroll
+    for (int p = 1; p < kMaxPeers; ++p) {
+      if (p < ntargets && w >= t.off[p]) q = p;
+    }
+    const int64_t row = ids[w];
+    if (row < 0 || row >= max_rows) continue;
+    const int4* s = reinterpret_cast<const int4*>(src) + row * row_words;
+    int4* d = reinterpret_cast<int4*>(t.dst[q]) + row * row_words;
+    for (int64_t k = lane; k < row_words; k += 32) d[k] = __ldg(s + k);
+  }
+}
+
+}  // namespace
+
+extern "C" int gnn_peer_push_rows(const void* src, void* const* dsts, int ndst, const int32_t* row_ids,
+                                  const int64_t* row_offsets, int64_t row_bytes, int64_t max_rows, int ctas,
+                                  gnn_stream_t stream) {
+  GNN_REQUIRE(ndst >= 0 && ndst <= kMaxPeers, GNN_ERR_INVALID_ARGUMENT,
+              "ndst must be in 0.." + std::to_string(kMaxPeers));
+  if (ndst == 0) {
+    clear_error();
+    return GNN_OK;
+  }
+  GNN_REQUIRE(dsts != nullptr && row_offsets != nullptr, GNN_ERR_NULL_POINTER,
+              "dsts and row_offsets must not be NULL");
+  ListedTargets t{};
+  t.off[0] = row_offsets[0];
+  GNN_REQUIRE(row_offsets[0] == 0, GNN_ERR_INVALID_ARGUMENT, "row_offsets must start at 0");
+  for (int p = 0; p < ndst; ++p) {
+    GNN_REQUIRE(row_offsets[p + 1] >= row_offsets[p], GNN_ERR_INVALID_ARGUMENT, "row_offsets must not decrease");
+    t.off[p + 1] = row_offsets[p + 1];
+  }
+  for (int p = ndst + 1; p <= kMaxPeers; ++p) t.off[p] = t.off[ndst];
+  const int64_t total = t.off[ndst];
+  if (total == 0) {
+    clear_error();
+    return GNN_OK;
+  }
+  GNN_REQUIRE(src != nullptr && row_ids != nullptr, GNN_ERR_NULL_POINTER, "src and row_ids must not be NULL");
+  GNN_REQUIRE(row_bytes > 0 && row_bytes % 16 == 0 && reinterpret_cast<uintptr_t>(src) % 16 == 0,
+              GNN_ERR_INVALID_ARGUMENT, "row_bytes and src must be multiples of 16");
+  GNN_REQUIRE(max_rows > 0, GNN_ERR_INVALID_ARGUMENT, "max_rows must be > 0");
+  for (int p = 0; p < ndst; ++p) {
+    GNN_REQUIRE(dsts[p] != nullptr && reinterpret_cast<uintptr_t>(dsts[p]) % 16 == 0, GNN_ERR_INVALID_ARGUMENT,
+                "every destination must be a 16-byte aligned, non-NULL pointer");
+    t.dst[p] = static_cast<char*>(dsts[p]);
+  }
+  const int64_t want = (total + 15) / 16;  // 16 warps per 512-thread CTA
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, ctas > 0 ? ctas : 4 * sm_count())));
+  push_listed_rows_kernel<<<grid, 512, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const char*>(src), t, ndst, row_ids, row_bytes / 16, max_rows);
+  GNN_LAUNCH_CHECK("peer row-list push kernel launch");
+  clear_error();
+  return GNN_OK;
+}

@@ -289,6 +289,61 @@ def make_padded_shard(row_ptr: torch.Tensor, col_ind: torch.Tensor, layout: Padd
     return PaddedShard(rank, pieces)
 
 
+@dataclass
+class HaloPlan:
+    """The rows of one rank that its peers read, per row piece: the halo push list.
+
+    For piece c, ``ids[c]`` (int32, device) holds padded row ids of this rank's
+    piece c, grouped by peer in ``peers`` order and sorted within a group;
+    peer ``peers[q]`` receives ids[c][offsets[c][q]:offsets[c][q+1]]. A peer
+    reads a remote row only through a column id of its CSR, so these are
+    exactly the rows it needs; the rest of its copy of the next layer's input
+    is never read and need not be sent.
+    """
+    rank: int
+    peers: list[int]
+    ids: list[torch.Tensor]
+    offsets: list[list[int]]
+
+    @property
+    def rows_sent(self) -> int:
+        return sum(o[-1] for o in self.offsets)
+
+
+def make_halo_plan(row_ptr: torch.Tensor, col_ind: torch.Tensor, layout: PaddedLayout, rank: int) -> HaloPlan:
+    """Halo lists of `rank` from the global CSR (global ids, any device): every
+    (peer, column) pair where a row owned by the peer reads a column owned by
+    `rank`, de-duplicated, as padded ids split by `rank`'s row pieces."""
+    dev = row_ptr.device
+    n, w, mc = layout.num_nodes, layout.world, layout.chunk_rows
+    owner = torch.empty(n, dtype=torch.int64, device=dev)
+    for r, o in enumerate(layout.order):
+        owner[o.to(dev)] = r
+    rp64 = row_ptr.to(torch.int64)
+    row_owner = owner.repeat_interleave(rp64[1:] - rp64[:-1])
+    col = col_ind.to(torch.int64)
+    sel = (owner[col] == rank) & (row_owner != rank)
+    pid = layout.padded_ids(col[sel])
+    total_rows = layout.padded_rows
+    key = torch.unique(row_owner[sel] * total_rows + pid)  # peer-major, then padded id
+    del owner, row_owner, col, sel, pid
+    peer_of = key // total_rows
+    ids = key - peer_of * total_rows
+    piece = ids // (w * mc)
+    peers = [p for p in range(w) if p != rank]
+    out_ids, out_off = [], []
+    for c in range(layout.chunks):
+        m = piece == c
+        ids_c, peer_c = ids[m], peer_of[m]
+        counts = torch.bincount(peer_c, minlength=w).cpu().tolist() if peer_c.numel() else [0] * w
+        off = [0]
+        for p in peers:
+            off.append(off[-1] + int(counts[p]))
+        out_ids.append(ids_c.to(torch.int32).contiguous())
+        out_off.append(off)
+    return HaloPlan(rank, peers, out_ids, out_off)
+
+
 def allgather_buffers(layout: PaddedLayout, feat: int, device) -> dict:
     """Buffers for gcn_forward_allgather: 'agg' [Mc, F], 'out' [chunks*Mc, F]
     (padding rows zero), 'x_next' [padded_rows, F]."""
@@ -459,6 +514,22 @@ class PeerRowExchange:
             N.call("gnn_copy_async", ctypes.c_void_p(self.peer_ptrs[self.turn][p] + off), ctypes.c_void_p(src),
                    nbytes, ctypes.c_void_p(s.cuda_stream))
 
+    def push_rows(self, ids: torch.Tensor, offsets: list[int], peers: list[int], ready: torch.cuda.Event) -> None:
+        """Halo push: send the listed rows of the current copy (ids[offsets[q]:offsets[q+1]]
+        to peers[q]) once `ready` has fired; one gnn_peer_push_rows kernel on the push stream."""
+        if offsets[-1] == 0 or not self.peer_ptrs[self.turn]:
+            return
+        if self.transport != "sm":
+            raise ValueError("halo pushes need the sm transport")
+        s = self.streams[-1]
+        s.wait_event(ready)
+        dsts = [self.peer_ptrs[self.turn][p] for p in peers]
+        arr = (ctypes.c_void_p * len(dsts))(*dsts)
+        offs = (ctypes.c_int64 * len(offsets))(*offsets)
+        N.call("gnn_peer_push_rows", ctypes.c_void_p(self.buffers[self.turn].data_ptr()), arr, len(dsts),
+               ctypes.c_void_p(ids.data_ptr()), offs, self.row_bytes, self.shape[0], self.ctas,
+               ctypes.c_void_p(s.cuda_stream))
+
     def finish(self) -> torch.Tensor:
         """Barrier after every rank's pushes; returns the completed copy and moves to the other one."""
         for s in self.streams.values():
@@ -487,14 +558,15 @@ class PeerRowExchange:
 
 def gcn_forward_push(shard: PaddedShard, dis_pad: torch.Tensor, x_pad: torch.Tensor, weights: list[torch.Tensor],
                      biases: list[torch.Tensor], layout: PaddedLayout, exchange: PeerRowExchange, agg: torch.Tensor,
-                     out: torch.Tensor, timers: dict | None = None) -> torch.Tensor:
+                     out: torch.Tensor, timers: dict | None = None, halo: HaloPlan | None = None) -> torch.Tensor:
     """Multi-layer GCN over a padded-layout shard; layer outputs pushed to the peers piece by piece.
 
     exchange: a PeerRowExchange over layout.padded_rows rows. agg: [Mc, F]
     scratch. out: [chunks*Mc, F] for the last layer (local order). Each piece's
     aggregation and X·W + b (+ReLU) land in this rank's rows of the exchange's
     current copy, which are then pushed to the peers while the next piece is
-    computed. Returns this rank's [rows, F] output rows (local order).
+    computed. With a `halo` plan only the rows each peer reads are pushed.
+    Returns this rank's [rows, F] output rows (local order).
     """
     layers = len(weights)
     mc = layout.chunk_rows
@@ -516,7 +588,10 @@ def gcn_forward_push(shard: PaddedShard, dis_pad: torch.Tensor, x_pad: torch.Ten
             if not last:
                 ready = torch.cuda.Event()
                 ready.record()
-                exchange.push(piece.row_begin, piece.row_end, ready)
+                if halo is None:
+                    exchange.push(piece.row_begin, piece.row_end, ready)
+                else:
+                    exchange.push_rows(halo.ids[c], halo.offsets[c], halo.peers, ready)
         if not last:
             h = exchange.finish()
     return out[:shard.num_rows]

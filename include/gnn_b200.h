@@ -410,6 +410,15 @@ int gnn_copy_async(void* dst, const void* src, size_t bytes, gnn_stream_t stream
  * NVLink writes. ctas limits the grid (0 = 4 per SM). bytes, src and every
  * destination must be 16-byte aligned. */
 int gnn_peer_push(const void* src, void* const* dsts, int ndst, size_t bytes, int ctas, gnn_stream_t stream);
+/* Halo push: stores only the rows each peer reads. For destination q, rows
+ * row_ids[row_offsets[q] .. row_offsets[q+1]) (row_offsets is a HOST array of
+ * ndst + 1 entries starting at 0; row_ids is device int32) are copied from src
+ * to the same row of dsts[q] (every buffer has the same [max_rows, row_bytes]
+ * layout). One warp per listed row; ids outside [0, max_rows) are skipped.
+ * row_bytes, src and every destination must be 16-byte aligned; ndst <= 8. */
+int gnn_peer_push_rows(const void* src, void* const* dsts, int ndst, const int32_t* row_ids,
+                       const int64_t* row_offsets, int64_t row_bytes, int64_t max_rows, int ctas,
+                       gnn_stream_t stream);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

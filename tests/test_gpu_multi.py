@@ -1,10 +1,11 @@
 """Row-partitioned multi-GPU GCN forward equals the single-GPU forward bit for bit.
 
-Covers the three exchanges: NCCL broadcast; NCCL all_gather on the padded
+Covers the exchanges: NCCL broadcast; NCCL all_gather on the padded
 chunk-major layout; pushes into the peers' IPC-mapped buffers by the SM push
-kernel and by copy engines (three steps in a row, so both alternating buffers
-are used) — on contiguous row ranges and on rows dealt to ranks by cost, with
-1 to 3 pieces per rank.
+kernel and by copy engines, and halo pushes of only the rows each peer reads
+(three steps in a row, so both alternating buffers are used, and the rows a
+halo push skips hold stale values that must never be read) — on contiguous
+row ranges and on rows dealt to ranks by cost, with 1 to 3 pieces per rank.
 
 Runs only where at least two GPUs are visible (spawned ranks, one GPU each,
 NCCL with NVLS off). The long-row threshold is fixed so every rank uses the
@@ -66,7 +67,8 @@ def _worker(rank, world, port, q):
         padded = []
         rp_np = rp.cpu().numpy()
         cases = [("allgather", None, 1, False), ("allgather", None, 3, True),
-                 ("push", "sm", 1, True), ("push", "ce", 3, True), ("push", "sm", 2, False)]
+                 ("push", "sm", 1, True), ("push", "ce", 3, True), ("push", "sm", 2, False),
+                 ("halo", "sm", 1, True), ("halo", "sm", 2, True), ("halo", "sm", 3, False)]
         for how, transport, chunks, balanced in cases:
             lay = partition.make_padded_layout(rp_np, world, chunks, balanced=balanced, row_cost=6)
             pshard = partition.make_padded_shard(rp, ci, lay, rank)
@@ -76,10 +78,11 @@ def _worker(rank, world, port, q):
                 pout = partition.gcn_forward_allgather(pshard, dis_p, x_p, ws, bs, lay, pbufs)
             else:
                 ex = partition.PeerRowExchange(lay.padded_rows, FEAT, rank, world, dev, transport=transport)
+                halo = partition.make_halo_plan(rp, ci, lay, rank) if how == "halo" else None
                 agg = torch.empty(lay.chunk_rows, FEAT, device=dev)
                 mine = torch.empty(lay.local_rows, FEAT, device=dev)
                 for _ in range(3):  # repeated steps alternate the two copies
-                    pout = partition.gcn_forward_push(pshard, dis_p, x_p, ws, bs, lay, ex, agg, mine)
+                    pout = partition.gcn_forward_push(pshard, dis_p, x_p, ws, bs, lay, ex, agg, mine, halo=halo)
             # collect the final rows through the same layout
             pfull = torch.zeros(lay.local_rows, FEAT, device=dev)
             pfull[:pshard.num_rows] = pout
@@ -88,7 +91,7 @@ def _worker(rank, world, port, q):
             for c in range(lay.chunks):
                 dist.all_gather_into_tensor(gathered[c * world * mc:(c + 1) * world * mc], pfull[c * mc:(c + 1) * mc])
             padded.append(lay.unpad_rows(gathered).cpu().numpy())
-            if how == "push":
+            if how in ("push", "halo"):
                 ex.close()
         torch.cuda.synchronize(dev)
         q.put((rank, full.cpu().numpy(), padded))

@@ -247,3 +247,45 @@ def test_two_rank_exchange_matches_single_rank():
     ref = O.spmm(g.row_ptr.numpy(), g.col_ind.numpy(), x.numpy(), mode=O.W_GCN, dis=g.deg_inv_sqrt.numpy())
     for r in range(2):
         assert np.array_equal(results[r].view(np.uint32), ref.view(np.uint32))
+
+
+@pytest.mark.parametrize("world,chunks,balanced", [(2, 1, True), (3, 2, True), (4, 3, False), (8, 2, True)])
+def test_halo_plan_delivers_every_row_a_rank_reads(world, chunks, balanced):
+    """Emulates the halo exchange on the CPU: every rank writes its own rows into
+    its copy of the next layer's input (the rest NaN), then each rank's listed
+    rows are copied into the listed peers' copies. Every row a rank's CSR reads
+    must then hold the true value — and nothing beyond the halo is sent."""
+    n = 3000
+    u, v = synth.rmat_undirected(n, n * 6, seed=71)
+    s, d = synth.symmetrize(u, v)
+    rp, ci, _ = synth.csr_on_device(s, d, n, add_self_loops=True)
+    lay = partition.make_padded_layout(rp.numpy(), world, chunks, balanced=balanced, row_cost=6)
+    truth = lay.pad_rows(torch.arange(n, dtype=torch.float32).unsqueeze(1) + 1.0)
+    ids_of = lay.ids
+    bufs = []
+    for r in range(world):
+        b = torch.full((lay.padded_rows, 1), float("nan"))
+        own = ids_of[lay.order[r]]
+        b[own] = truth[own]
+        bufs.append(b)
+    plans = [partition.make_halo_plan(rp, ci, lay, r) for r in range(world)]
+    for r, plan in enumerate(plans):
+        assert plan.peers == [p for p in range(world) if p != r]
+        for c in range(lay.chunks):
+            off = plan.offsets[c]
+            assert len(off) == world and off[0] == 0
+            ids = plan.ids[c].to(torch.int64)
+            lo, hi = lay.piece_first(r, c), lay.piece_first(r, c) + lay.chunk_rows
+            assert bool(((ids >= lo) & (ids < hi)).all()), "listed rows must be the sender's piece c"
+            for q, p in enumerate(plan.peers):
+                seg = ids[off[q]:off[q + 1]]
+                assert bool((seg[1:] > seg[:-1]).all()), "sorted, no duplicates"
+                bufs[p][seg] = bufs[r][seg]
+    sent = 0
+    for r in range(world):
+        shard = partition.make_padded_shard(rp, ci, lay, r)
+        cols = torch.cat([pc.col_ind.to(torch.int64) for pc in shard.pieces])
+        assert torch.equal(bufs[r][cols], truth[cols]), f"rank {r} reads a row that was not delivered"
+        own = set(ids_of[lay.order[r]].tolist())
+        sent += len(set(cols.tolist()) - own)
+    assert sent == sum(p.rows_sent for p in plans)
