@@ -158,6 +158,8 @@ def run_gin_inference(*, framework_label: str, select_device: Callable[[str], to
         if device.type == "cuda":
             torch.cuda.synchronize(device)
         phases.reset()
+        if capture is not None and capture.get("on_measure_begin"):
+            capture["on_measure_begin"]()
         D.cuda_profiler(device, True)
         start = time.perf_counter()
         output = features
@@ -168,6 +170,8 @@ def run_gin_inference(*, framework_label: str, select_device: Callable[[str], to
         if device.type == "cuda":
             torch.cuda.synchronize(device)
         elapsed = time.perf_counter() - start
+        if capture is not None and capture.get("on_measure_end"):
+            capture["on_measure_end"]()
         D.cuda_profiler(device, False)
 
     print(f"Graph:\t{graph_path}")
@@ -186,6 +190,9 @@ def run_gin_inference(*, framework_label: str, select_device: Callable[[str], to
     print(D.describe_memory("weights1_l0", layers[0].weight1))
     print(D.describe_memory("output", output))
     if capture is not None:  # test hook: the final output and everything needed to recompute it
+        capture.update(feature_range=(int(features.data_ptr()),
+                                      int(features.data_ptr()) + features.numel() * features.element_size()),
+                       spmm_avg_ns=phases.avg_ns("spmm", iters=int(args.iters)), iters=int(args.iters))
         capture.update(output=output.detach().cpu(), features=features.detach().cpu(), layers=layers,
                        row_ptr=row_ptr.detach().cpu(), col_ind=col_ind.detach().cpu(), num_nodes=num_nodes)
     print(f"Output Sum:\t{float(output.sum().item()):.6f}")

@@ -88,7 +88,36 @@ def build(verbose: bool = False, ptxas_info: bool = False, force: bool = False) 
             sys.stderr.write(" ".join(cmd) + "\n" + res.stdout + res.stderr)
             raise RuntimeError("link of libgnnb200.so failed")
         os.replace(tmp, LIB)
+    build_umprof()
     return LIB
+
+
+UMPROF_SRC = PKG / "csrc_prof" / "um_profiler.cpp"
+UMPROF_LIB = PKG / "libgnnb200_umprof.so"
+
+
+def _cuda_root() -> Path:
+    return Path(_nvcc()).resolve().parent.parent
+
+
+def build_umprof(force: bool = False) -> Path:
+    """libgnnb200_umprof.so: the CUPTI unified-memory counter library (host code
+    only, linked against the toolkit's libcupti with an rpath to it)."""
+    deps = [UMPROF_SRC, INCLUDE / "gnn_b200_umprof.h", INCLUDE / "gnn_b200.h", Path(__file__)]
+    if not force and UMPROF_LIB.exists() and all(p.stat().st_mtime <= UMPROF_LIB.stat().st_mtime for p in deps):
+        return UMPROF_LIB
+    cuda = _cuda_root()
+    libdir = cuda / "lib64"
+    tmp = UMPROF_LIB.with_suffix(".so.tmp")
+    cmd = [os.environ.get("CXX", "g++"), "-O2", "-std=c++17", "-shared", "-fPIC", "-fvisibility=hidden",
+           f"-I{INCLUDE}", f"-I{cuda / 'include'}", str(UMPROF_SRC), "-o", str(tmp), f"-L{libdir}", "-lcupti",
+           f"-Wl,-rpath,{libdir}", "-Wl,--exclude-libs,ALL"]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        sys.stderr.write(" ".join(cmd) + "\n" + res.stdout + res.stderr)
+        raise RuntimeError("build of libgnnb200_umprof.so failed")
+    os.replace(tmp, UMPROF_LIB)
+    return UMPROF_LIB
 
 
 def main() -> int:

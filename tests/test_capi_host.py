@@ -125,3 +125,18 @@ def test_locality_arguments_rejected_without_device():
     assert L.gnn_locality_count_histogram(None, 0, None, 0, None) == 1
     assert L.gnn_permute_edges(None, None, 0, None, 5, None, None, None, 0, None) == 0
     assert L.gnn_permute_edges(None, None, 4, None, 5, None, None, None, 0, None) == 2
+
+
+def test_um_profiler_library_exports_its_header():
+    from gnn_cuda_b200.GNN_cuda_common import um_profiler as U
+    text = (ROOT / "include" / "gnn_b200_umprof.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    names = sorted(set(re.findall(r"\b(gnn_um_[a-z0-9_]+)\s*\(", text)))
+    assert len(names) == 7 and set(names) == set(U.PROTOTYPES)
+    lib = ctypes.CDLL(str(U.LIB_PATH))
+    assert all(hasattr(lib, n) for n in names)
+    # argument checks need no device
+    out = U.gnn_um_totals()
+    assert U.lib().gnn_um_profiler_totals(5, 1, 0, 0, ctypes.byref(out)) == 1
+    assert U.lib().gnn_um_profiler_totals(0, 0, 0, 0, None) == 2
+    assert U.lib().gnn_um_profiler_totals(0, 0, 0, 0, ctypes.byref(out)) == 0 and out.records == 0
