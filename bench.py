@@ -76,9 +76,10 @@ def parse_args():
     ap.add_argument("--push-ctas", type=int, default=0, help="grid of the SM push kernel (0: 4 per SM)")
     ap.add_argument("--layout", choices=["balanced", "contiguous"], default="balanced",
                     help="N > 1: rows dealt to ranks by cost, or contiguous cost-balanced ranges")
-    ap.add_argument("--workload", choices=["gcn_products_like", "locality_products_like"],
+    ap.add_argument("--workload", choices=["gcn_products_like", "sage_reddit_like", "locality_products_like"],
                     default="gcn_products_like",
-                    help="the GCN forward (default), or the UVM locality preprocessing of the same graph (1 GPU)")
+                    help="the GCN forward (default); the GraphSAGE-mean forward on the Reddit-shaped graph (1 GPU); "
+                         "or the UVM locality preprocessing of the products-shaped graph (1 GPU)")
     return ap.parse_args()
 
 
@@ -446,6 +447,116 @@ def run_reference(args, device: torch.device):
 
 
 # ---------------------------------------------------------------------------
+# GraphSAGE-mean workload (Reddit-shaped graph, 2 layers 256 -> 256 -> 256)
+# ---------------------------------------------------------------------------
+
+SAGE_FEAT = 256
+
+
+def mean_layer_bytes(n: int, nnz: int, f: int) -> int:
+    """Algorithmic bytes of one mean aggregation: row_ptr + col_ind + one gathered
+    feature row per CSR entry + the output matrix."""
+    return (n + 1) * 4 + nnz * 4 + nnz * f * 4 + n * f * 4
+
+
+def run_sage(args, device: torch.device) -> dict:
+    """graphsage_inference.py's layer, per layer: mean aggregation, agg·W_n + b_n,
+    x·W_r, add, ReLU between layers — the reference's composition
+    (graphsage_inference.py:310-354) on this library's kernels."""
+    t0 = time.time()
+    src, dst, n = synth.make_graph("sage_reddit_like", seed=args.seed, device=device, scale_nodes=args.scale)
+    rp, ci, _ = synth.csr_on_device(src, dst, n, add_self_loops=False)
+    del src, dst
+    nnz = int(ci.numel())
+    x = synth.features(n, SAGE_FEAT, seed=args.seed + 1, device=device)
+    wn = [synth.glorot(SAGE_FEAT, SAGE_FEAT, seed=args.seed + 10 + i, device=device) for i in range(LAYERS)]
+    wr = [synth.glorot(SAGE_FEAT, SAGE_FEAT, seed=args.seed + 20 + i, device=device) for i in range(LAYERS)]
+    bn = [torch.zeros(SAGE_FEAT, device=device) for _ in range(LAYERS)]
+    agg = torch.empty(n, SAGE_FEAT, device=device)
+    root = torch.empty(n, SAGE_FEAT, device=device)
+    outs = [torch.empty(n, SAGE_FEAT, device=device) for _ in range(2)]
+    torch.cuda.empty_cache()
+    torch.cuda.synchronize(device)
+    log(f"[bench] sage graph n={n} nnz={nnz} built in {time.time() - t0:.1f}s")
+    torch.backends.cuda.matmul.allow_tf32 = True
+    timers: dict = {}
+
+    def step(tm=None):
+        h = x
+        for li in range(LAYERS):
+            ev = partition._mark(tm, "spmm_begin")
+            agg_ops.spmm_mean_forward_(rp, ci, h, agg)
+            partition._mark(tm, "spmm_end", ev)
+            o = outs[li % 2]
+            agg_ops.linear_forward_(agg, wn[li], bn[li], o, False)
+            agg_ops.gemm_forward_(h, wr[li], root)
+            agg_ops.tensor_add_inplace_(o, root, 1.0)
+            if li != LAYERS - 1:
+                agg_ops.relu_inplace_(o)
+            h = o
+        return h
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(device)
+    launches0 = N.lib().gnn_kernel_launches()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device.index) as clocks:
+        e0.record()
+        for _ in range(args.steps):
+            step(timers)
+        e1.record()
+        torch.cuda.synchronize(device)
+    launches = N.lib().gnn_kernel_launches() - launches0
+    ms_step = e0.elapsed_time(e1) / args.steps
+    spmm_ms = sum(b.elapsed_time(e) for b, e in timers["spmm"]) / (args.steps * LAYERS)
+    bytes_layer = mean_layer_bytes(n, nnz, SAGE_FEAT)
+    # e2e through the public ops with host buffers
+    dev_in = [rp, ci, x] + wn + wr + bn
+    host_in = [t.cpu().pin_memory() for t in dev_in]
+    out_host = torch.empty(n, SAGE_FEAT, pin_memory=True)
+    torch.cuda.synchronize(device)
+    q0 = torch.cuda.Event(enable_timing=True)
+    q1 = torch.cuda.Event(enable_timing=True)
+    q0.record()
+    for _ in range(args.e2e_steps):
+        for d_t, h_t in zip(dev_in, host_in):
+            d_t.copy_(h_t, non_blocking=True)
+        out_host.copy_(step(), non_blocking=True)
+    q1.record()
+    torch.cuda.synchronize(device)
+    e2e_ms = q0.elapsed_time(q1) / args.e2e_steps
+    peak, peak_kind = measured_hbm_gbs()
+    achieved = bytes_layer / (spmm_ms * 1e-3) / 1e9
+    res = {
+        "metric": METRIC, "value": round(bytes_layer * LAYERS / (ms_step * 1e-3) / 1e9, 2), "unit": "GB/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+        "ms_per_layer": round(ms_step / LAYERS, 4), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "fp32",
+        "data": f"synthetic: seeded log-normal community graph (seed {args.seed}) with Reddit shape, N(0,1) "
+                "features, Glorot weights, zero bias",
+        "config": {"workload": "sage_reddit_like: GraphSAGE-mean 2 layers 256->256->256 (self || mean-neighbour "
+                               "linear, ReLU between layers)", "nodes": n, "csr_entries": nnz, "feat_dim": SAGE_FEAT,
+                   "layers": LAYERS, "self_loops": False,
+                   "gemm": "tcgen05-tf32" if N.lib().gnn_gemm_uses_tensor_cores(n, SAGE_FEAT, SAGE_FEAT)
+                   else "ffma-fp32",
+                   "l2": "X is %.2f GB (reused ~%d times per layer), no flush" % (n * SAGE_FEAT * 4 / 1e9,
+                                                                                 nnz // max(1, n))},
+        "roofline": {"bound": "hbm", "kernel": "spmm_vec_kernel + spmm_long_kernel (mean aggregation)",
+                     "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                     "peak_source": peak_kind, "spmm_ms_per_layer": round(spmm_ms, 4),
+                     "algorithmic_bytes_per_layer": bytes_layer, "traffic": None},
+        "e2e": {"value": round(bytes_layer * LAYERS / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "h2d_bytes_per_step": int(sum(t.numel() * t.element_size() for t in host_in)),
+                "d2h_bytes_per_step": int(out_host.numel() * 4), "ms_per_step": round(e2e_ms, 3),
+                "api": "gnn_cuda_b200.GNN_cuda_common.agg_ops over libgnnb200.so"},
+        "gpu_launches": int(launches), "clocks": clocks.summary(),
+    }
+    return res
+
+
+# ---------------------------------------------------------------------------
 # locality preprocessing workload (the input of spmm_mode=optimized)
 # ---------------------------------------------------------------------------
 
@@ -528,6 +639,15 @@ def main() -> int:
         log(f"[bench] WORLD_SIZE={world} but --gpus={args.gpus}; using WORLD_SIZE")
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
+    if args.workload == "sage_reddit_like":
+        if rank != 0:
+            return 0
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the CPU reference arm is measured on the "
+                              "default workload (gcn_products_like)"}), flush=True)
+        else:
+            print(json.dumps(run_sage(args, device)), flush=True)
+        return 0
     if args.workload == "locality_products_like":
         if rank != 0:
             return 0
