@@ -24,7 +24,17 @@ import torch
 
 from .. import _native as N
 from . import native_ops
-from .graph_utils import device_csr, feature_rows_per_page
+
+
+def device_csr(*args, **kwargs):
+    # graph_utils re-exports this module's functions, so it is imported on use, not at import time
+    from .graph_utils import device_csr as build
+    return build(*args, **kwargs)
+
+
+def feature_rows_per_page(**kwargs) -> int:
+    from .graph_utils import feature_rows_per_page as rows
+    return rows(**kwargs)
 
 
 def _compute_device(*ts) -> torch.device:

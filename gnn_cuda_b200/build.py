@@ -111,7 +111,7 @@ def build_umprof(force: bool = False) -> Path:
     tmp = UMPROF_LIB.with_suffix(".so.tmp")
     cmd = [os.environ.get("CXX", "g++"), "-O2", "-std=c++17", "-shared", "-fPIC", "-fvisibility=hidden",
            f"-I{INCLUDE}", f"-I{cuda / 'include'}", str(UMPROF_SRC), "-o", str(tmp), f"-L{libdir}", "-lcupti",
-           f"-Wl,-rpath,{libdir}", "-Wl,--exclude-libs,ALL"]
+           f"-Wl,-rpath,{libdir}", "-Wl,--exclude-libs,ALL", "-ldl"]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         sys.stderr.write(" ".join(cmd) + "\n" + res.stdout + res.stderr)

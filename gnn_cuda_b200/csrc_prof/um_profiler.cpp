@@ -17,6 +17,7 @@
 // It is a separate shared library (libgnnb200_umprof.so) so that the aggregation
 // library itself never depends on CUPTI.
 #include <cupti.h>
+#include <dlfcn.h>
 
 #include <algorithm>
 #include <cstdint>
@@ -98,6 +99,21 @@ bool overlaps_window(const Record& r, uint64_t t0, uint64_t t1) {
   return r.start < t1 && end > t0;
 }
 
+// CUPTI enables the unified-memory counters only once the driver API is
+// initialised (cuptiActivityEnable answers CUPTI_ERROR_NOT_READY before).
+// cuInit creates no context; it is looked up at run time so that this library
+// has no link-time dependency on the driver.
+int init_driver() {
+  void* h = dlopen("libcuda.so.1", RTLD_NOW | RTLD_GLOBAL);
+  if (h == nullptr) return fail(GNN_ERR_DEVICE, "libcuda.so.1 not found: no NVIDIA driver");
+  using InitFn = int (*)(unsigned int);
+  auto init = reinterpret_cast<InitFn>(dlsym(h, "cuInit"));
+  if (init == nullptr) return fail(GNN_ERR_DEVICE, "cuInit not found in libcuda.so.1");
+  const int rc = init(0);
+  if (rc != 0) return fail(GNN_ERR_DEVICE, "cuInit failed with driver error " + std::to_string(rc));
+  return GNN_OK;
+}
+
 }  // namespace
 
 extern "C" int gnn_um_profiler_start(void) {
@@ -106,6 +122,8 @@ extern "C" int gnn_um_profiler_start(void) {
     g_error.clear();
     return GNN_OK;
   }
+  const int drc = init_driver();
+  if (drc != GNN_OK) return drc;
   CUptiResult r;
   if (!g_registered) {
     r = cuptiActivityRegisterCallbacks(buffer_requested, buffer_completed);

@@ -45,6 +45,8 @@ print(json.dumps(out))
 
 def test_um_counters_see_migrations_and_faults():
     res = subprocess.run([sys.executable, "-c", _TOUCH, str(ROOT)], capture_output=True, text=True, timeout=300)
+    if "UM_PROFILING_NOT_SUPPORTED" in res.stderr:
+        pytest.skip("CUPTI reports unified-memory profiling unsupported on this system")
     assert res.returncode == 0, res.stderr[-3000:]
     out = json.loads(res.stdout.strip().splitlines()[-1])
     size = 64 * 2**20
