@@ -66,7 +66,7 @@ def ensure_workspace(device: torch.device, num_nodes: int, num_edges: int) -> No
     """Allocate the aggregation workspace of the current stream now (e.g. before a
     caller reserves the rest of device memory), so later calls allocate nothing."""
     with torch.cuda.device(device):
-        _workspace(device, N.lib().gnn_spmm_workspace_bytes(int(num_nodes), int(num_edges)))
+        _workspace(device, N.lib().gnn_spmm_schedule_workspace_bytes(int(num_nodes), int(num_edges)))
 
 
 def _index_type(row_ptr: torch.Tensor) -> int:
@@ -127,7 +127,7 @@ def _spmm_call(fn_name: str, row_ptr, col_ind, vec, x, out, *extra_args, optimiz
     dev = out.device
     with torch.cuda.device(dev):
         rp, ci, vp, xp = _dev_ptr(row_ptr), _dev_ptr(col_ind), _dev_ptr(vec), _dev_ptr(x)
-        ws, wsb = _workspace(dev, N.lib().gnn_spmm_workspace_bytes(n, nnz))
+        ws, wsb = _workspace(dev, N.lib().gnn_spmm_schedule_workspace_bytes(n, nnz))
         s = _stream(dev)
         fn = getattr(N.lib(), fn_name)
         if optimized is not None:

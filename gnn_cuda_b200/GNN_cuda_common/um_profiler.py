@@ -42,6 +42,7 @@ PROTOTYPES = {
     "gnn_um_profiler_timestamp": (ctypes.c_uint64, []),
     "gnn_um_profiler_totals": (ctypes.c_int, [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64,
                                               ctypes.POINTER(gnn_um_totals)]),
+    "gnn_um_profiler_enabled_kinds": (ctypes.c_int, []),
     "gnn_um_profiler_last_error": (ctypes.c_char_p, []),
 }
 
@@ -82,6 +83,11 @@ class UMProfiler:
     def start(self) -> "UMProfiler":
         _check(lib().gnn_um_profiler_start(), "gnn_um_profiler_start")
         return self
+
+    @staticmethod
+    def enabled_kinds() -> int:
+        """Counter kinds collected: 7 = all, 3 = HtoD/DtoH/GPU faults, 2 = HtoD/DtoH."""
+        return int(lib().gnn_um_profiler_enabled_kinds())
 
     def flush(self) -> None:
         _check(lib().gnn_um_profiler_flush(), "gnn_um_profiler_flush")

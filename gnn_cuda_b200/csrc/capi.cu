@@ -80,6 +80,10 @@ extern "C" int gnn_config_set_int(const char* name, int64_t value) {
   } else if (std::strcmp(name, "spmm.kernel") == 0) {
     GNN_REQUIRE(value >= 0 && value <= 2, GNN_ERR_INVALID_ARGUMENT, "spmm.kernel must be 0, 1 or 2");
     config().spmm_kernel.store(value);
+  } else if (std::strcmp(name, "gemm.stages") == 0) {
+    GNN_REQUIRE(value == 0 || (value >= 2 && value <= 8), GNN_ERR_INVALID_ARGUMENT,
+                "gemm.stages must be 0 (automatic) or in [2, 8]");
+    config().gemm_stages.store(value);
   } else {
     return fail(GNN_ERR_INVALID_ARGUMENT, std::string("unknown config key: ") + name);
   }
@@ -95,6 +99,8 @@ extern "C" int gnn_config_get_int(const char* name, int64_t* value) {
     *value = config().long_row_warps.load();
   } else if (std::strcmp(name, "spmm.kernel") == 0) {
     *value = config().spmm_kernel.load();
+  } else if (std::strcmp(name, "gemm.stages") == 0) {
+    *value = config().gemm_stages.load();
   } else {
     return fail(GNN_ERR_INVALID_ARGUMENT, std::string("unknown config key: ") + name);
   }

@@ -56,6 +56,7 @@ struct Config {
   std::atomic<int64_t> long_row_threshold{0};  // 0 = automatic
   std::atomic<int64_t> long_row_warps{16};
   std::atomic<int64_t> spmm_kernel{1};  // 0 packed stream, 1 one warp per row (default), 2 cp.async staging
+  std::atomic<int64_t> gemm_stages{0};  // tcgen05 GEMM X-tile ring depth; 0 = as deep as shared memory allows
 };
 Config& config();
 

@@ -41,6 +41,7 @@ std::vector<Record> g_records;
 uint64_t g_dropped = 0;
 bool g_registered = false;
 bool g_enabled = false;
+size_t g_kinds = 0;  // counter kinds enabled: a prefix of kKinds
 thread_local std::string g_error;
 
 constexpr size_t kBufferBytes = 8u << 20;
@@ -130,18 +131,40 @@ extern "C" int gnn_um_profiler_start(void) {
     if (r != CUPTI_SUCCESS) return cupti_fail(r, "cuptiActivityRegisterCallbacks");
     g_registered = true;
   }
-  CUpti_ActivityUnifiedMemoryCounterConfig cfg[sizeof(kKinds) / sizeof(kKinds[0])];
-  std::memset(cfg, 0, sizeof(cfg));
-  for (size_t i = 0; i < sizeof(kKinds) / sizeof(kKinds[0]); ++i) {
-    cfg[i].scope = CUPTI_ACTIVITY_UNIFIED_MEMORY_COUNTER_SCOPE_PROCESS_SINGLE_DEVICE;
-    cfg[i].kind = kKinds[i];
-    cfg[i].deviceId = 0;
-    cfg[i].enable = 1;
+  // Not every counter kind exists on every platform (the driver rejects the
+  // enable with CUPTI_ERROR_INVALID_PARAMETER when one does not), so the kinds
+  // are tried from the full set down to the ones the migration report needs.
+  constexpr size_t nk = sizeof(kKinds) / sizeof(kKinds[0]);
+  const size_t tiers[] = {nk, 3 /* HtoD, DtoH, GPU faults */, 2 /* HtoD, DtoH */};
+  CUptiResult last = CUPTI_SUCCESS;
+  const CUpti_ActivityUnifiedMemoryCounterScope scopes[] = {
+      CUPTI_ACTIVITY_UNIFIED_MEMORY_COUNTER_SCOPE_PROCESS_SINGLE_DEVICE,
+      CUPTI_ACTIVITY_UNIFIED_MEMORY_COUNTER_SCOPE_PROCESS_ALL_DEVICES};
+  r = CUPTI_ERROR_UNKNOWN;
+  for (size_t want : tiers) {
+    for (CUpti_ActivityUnifiedMemoryCounterScope scope : scopes) {
+      CUpti_ActivityUnifiedMemoryCounterConfig cfg[nk];
+      std::memset(cfg, 0, sizeof(cfg));
+      for (size_t i = 0; i < nk; ++i) {
+        cfg[i].scope = scope;
+        cfg[i].kind = kKinds[i];
+        cfg[i].deviceId = 0;
+        cfg[i].enable = i < want ? 1 : 0;
+      }
+      r = cuptiActivityConfigureUnifiedMemoryCounter(cfg, static_cast<uint32_t>(nk));
+      if (r == CUPTI_SUCCESS) r = cuptiActivityEnable(CUPTI_ACTIVITY_KIND_UNIFIED_MEMORY_COUNTER);
+      if (r == CUPTI_SUCCESS) break;
+      last = r;
+      if (r == CUPTI_ERROR_UM_PROFILING_NOT_SUPPORTED || r == CUPTI_ERROR_UM_PROFILING_NOT_SUPPORTED_ON_DEVICE) {
+        return cupti_fail(r, "enabling CUPTI unified-memory counters");
+      }
+    }
+    if (r == CUPTI_SUCCESS) {
+      g_kinds = want;
+      break;
+    }
   }
-  r = cuptiActivityConfigureUnifiedMemoryCounter(cfg, sizeof(kKinds) / sizeof(kKinds[0]));
-  if (r != CUPTI_SUCCESS) return cupti_fail(r, "cuptiActivityConfigureUnifiedMemoryCounter");
-  r = cuptiActivityEnable(CUPTI_ACTIVITY_KIND_UNIFIED_MEMORY_COUNTER);
-  if (r != CUPTI_SUCCESS) return cupti_fail(r, "cuptiActivityEnable(UNIFIED_MEMORY_COUNTER)");
+  if (r != CUPTI_SUCCESS) return cupti_fail(last, "enabling CUPTI unified-memory counters");
   g_enabled = true;
   g_error.clear();
   return GNN_OK;
@@ -225,6 +248,11 @@ extern "C" int gnn_um_profiler_totals(uint64_t range_begin, uint64_t range_end, 
   *out = s;
   g_error.clear();
   return GNN_OK;
+}
+
+extern "C" int gnn_um_profiler_enabled_kinds(void) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  return static_cast<int>(g_kinds);
 }
 
 extern "C" const char* gnn_um_profiler_last_error(void) { return g_error.c_str(); }

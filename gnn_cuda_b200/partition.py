@@ -83,7 +83,7 @@ def spmm_gcn_shard(shard: RowShard, deg_inv_sqrt: torch.Tensor, x_full: torch.Te
     assert out.shape == (shard.num_rows, x_full.shape[1]) and out.is_contiguous() and x_full.is_contiguous()
     dev = out.device
     idx = N.GNN_INDEX_INT64 if shard.row_ptr.dtype == torch.int64 else N.GNN_INDEX_INT32
-    ws, wsb = native_ops._workspace(dev, N.lib().gnn_spmm_workspace_bytes(shard.num_rows, shard.num_edges))
+    ws, wsb = native_ops._workspace(dev, N.lib().gnn_spmm_schedule_workspace_bytes(shard.num_rows, shard.num_edges))
     N.call("gnn_spmm_gcn_partition_forward", shard.row_ptr.data_ptr(), idx, shard.col_ind.data_ptr(),
            deg_inv_sqrt.data_ptr(), shard.row_begin, x_full.data_ptr(), out.data_ptr(), shard.num_rows,
            x_full.shape[0], shard.num_edges, x_full.shape[1], ws, wsb, native_ops._stream(dev))

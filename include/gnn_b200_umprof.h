@@ -54,6 +54,10 @@ uint64_t gnn_um_profiler_timestamp(void);
  * [t_begin, t_end) (0, 0 = all time). Call gnn_um_profiler_flush first. */
 int gnn_um_profiler_totals(uint64_t range_begin, uint64_t range_end, uint64_t t_begin, uint64_t t_end,
                            gnn_um_totals* out);
+/* Number of counter kinds collection runs with, as a prefix of: HtoD bytes,
+ * DtoH bytes, GPU page faults, CPU page faults, thrashing, throttling, remote
+ * maps (platforms lacking a kind run with fewer; at least the first two). */
+int gnn_um_profiler_enabled_kinds(void);
 const char* gnn_um_profiler_last_error(void);
 
 #if defined(__GNUC__)

@@ -132,7 +132,7 @@ def test_um_profiler_library_exports_its_header():
     text = (ROOT / "include" / "gnn_b200_umprof.h").read_text()
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
     names = sorted(set(re.findall(r"\b(gnn_um_[a-z0-9_]+)\s*\(", text)))
-    assert len(names) == 7 and set(names) == set(U.PROTOTYPES)
+    assert len(names) == 8 and set(names) == set(U.PROTOTYPES)
     lib = ctypes.CDLL(str(U.LIB_PATH))
     assert all(hasattr(lib, n) for n in names)
     # argument checks need no device

@@ -341,3 +341,51 @@ def test_multi_segment_hubs_all_kernels(f):
     status = ctypes.c_int(-1)  # no segment gave up waiting for its predecessor
     N.check(N.lib().gnn_device_status(1, ctypes.byref(status)))
     assert status.value == 0
+
+
+@pytest.mark.parametrize("idx", [torch.int32, torch.int64])
+def test_degree_schedule_matches_row_order_and_oracle(idx):
+    """With the schedule-sized workspace the per-row kernel takes rows in descending
+    degree order (counting sort per call); with the minimum workspace it takes
+    them in id order. Both must equal the oracle bit for bit (each row is still
+    summed alone in CSR order), for every weight mode, on a graph large enough
+    (>= 65,536 rows) for the schedule to be built."""
+    n, f = 150_000, 128
+    s, d = _graph("rmat", n, seed=31)
+    rp, ci, dis = O.gcn_normalized_csr(s.numpy(), d.numpy(), n)
+    x = synth.features(n, f, seed=32).numpy()
+    t = {k: torch.from_numpy(v).to(DEV) for k, v in dict(rp=rp, ci=ci, dis=dis, x=x).items()}
+    t["rp"] = t["rp"].to(idx)
+    L = N.lib()
+    nnz = int(ci.size)
+    small = int(L.gnn_spmm_workspace_bytes(n, nnz))
+    big = int(L.gnn_spmm_schedule_workspace_bytes(n, nnz))
+    assert big > small + n * 4 - 1
+    it = N.GNN_INDEX_INT64 if idx == torch.int64 else N.GNN_INDEX_INT32
+    stream = torch.cuda.current_stream(DEV).cuda_stream
+    old = [N.config_get(k) for k in ("spmm.kernel", "spmm.long_row_threshold", "spmm.long_row_warps")]
+    N.config_set("spmm.kernel", 1)
+    N.config_set("spmm.long_row_threshold", 256)
+    N.config_set("spmm.long_row_warps", 16)
+    try:
+        for mode, exp in (("gcn", O.spmm(rp, ci, x, mode=O.W_GCN, dis=dis, split_warps=16, long_thr=256)),
+                          ("sum", O.spmm(rp, ci, x, mode=O.W_UNIT, split_warps=16, long_thr=256))):
+            outs = []
+            for nbytes in (small, big):
+                ws = torch.empty(nbytes, dtype=torch.uint8, device=DEV)
+                o = torch.full((n, f), float("nan"), device=DEV)
+                if mode == "gcn":
+                    rc = L.gnn_spmm_gcn_forward(t["rp"].data_ptr(), it, t["ci"].data_ptr(), t["dis"].data_ptr(),
+                                                t["x"].data_ptr(), o.data_ptr(), n, nnz, f, ws.data_ptr(), nbytes,
+                                                ctypes.c_void_p(stream))
+                else:
+                    rc = L.gnn_spmm_sum_forward(t["rp"].data_ptr(), it, t["ci"].data_ptr(), t["x"].data_ptr(),
+                                                o.data_ptr(), n, nnz, f, ws.data_ptr(), nbytes,
+                                                ctypes.c_void_p(stream))
+                N.check(rc)
+                outs.append(o.cpu().numpy())
+            for o in outs:
+                assert _bits_equal(o, exp), mode
+    finally:
+        for k, v in zip(("spmm.kernel", "spmm.long_row_threshold", "spmm.long_row_warps"), old):
+            N.config_set(k, v)

@@ -36,7 +36,8 @@ for prefetch in (False, True):
     torch.cuda.synchronize()
     prof.flush()
     lo = t.data_ptr(); hi = lo + n * 4
-    out["prefetch" if prefetch else "touch"] = dict(prof.totals((lo, hi)), ok=(s == float(host.sum().item())))
+    out["prefetch" if prefetch else "touch"] = dict(prof.totals((lo, hi)), ok=(s == float(host.sum().item())),
+                                                    kinds=UMProfiler.enabled_kinds())
     del t
 prof.stop()
 print(json.dumps(out))
@@ -53,6 +54,7 @@ def test_um_counters_see_migrations_and_faults():
     touch, pre = out["touch"], out["prefetch"]
     assert touch["ok"] and pre["ok"]
     # first touch on the GPU migrates the pages host -> device through page faults
+    assert touch["kinds"] >= 3, "GPU page-fault counters are needed for the migration report"
     assert touch["htod_bytes"] >= 0.9 * size and touch["gpu_page_faults"] > 0
     # a prefetch migrates them ahead of the kernel: same bytes, (almost) no faults
     assert pre["htod_bytes"] >= 0.9 * size
