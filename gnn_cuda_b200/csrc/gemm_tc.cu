@@ -34,7 +34,8 @@ namespace {
 
 constexpr int BM = 128;             // rows per tile (TMEM lanes)
 constexpr int KCHUNK = 32;          // tf32 elements per 128-byte swizzle row
-constexpr int STAGES = 4;           // X chunk ring depth
+constexpr int MAX_STAGES = 8;       // X chunk ring depth: runtime, up to this many 16 KiB stages
+constexpr size_t kSmemLimit = 227 * 1024;
 constexpr int A_STAGE_BYTES = BM * KCHUNK * 4;  // 16 KiB
 constexpr int kThreads = 192;       // warp0 TMA, warp1 MMA/TMEM, warps 2-5 epilogue
 constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 2 GHz
@@ -49,6 +50,7 @@ struct TcParams {
   const float* bias;
   float* out;
   int relu;
+  int stages;  // X chunk ring depth (2..MAX_STAGES)
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -165,14 +167,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int kchunks = K / KCHUNK;
   const uint32_t w_bytes = static_cast<uint32_t>(BN) * K * 4;
   uint8_t* sW = smem;                                  // K/32 blocks of [BN rows x 128 B], K-major
-  uint8_t* sA = smem + ((w_bytes + 1023) & ~1023u);    // STAGES x 16 KiB
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sA + STAGES * A_STAGE_BYTES);
-  uint64_t* full = bars;                 // [STAGES]
-  uint64_t* empty = bars + STAGES;       // [STAGES]
-  uint64_t* acc_full = bars + 2 * STAGES;      // [2]
-  uint64_t* acc_empty = bars + 2 * STAGES + 2; // [2]
-  uint64_t* drain = bars + 2 * STAGES + 5;     // [1]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 6);
+  const int S = p.stages;
+  uint8_t* sA = smem + ((w_bytes + 1023) & ~1023u);    // S x 16 KiB
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sA + S * A_STAGE_BYTES);
+  uint64_t* full = bars;                 // [S]
+  uint64_t* empty = bars + S;            // [S]
+  uint64_t* acc_full = bars + 2 * S;     // [2]
+  uint64_t* acc_empty = bars + 2 * S + 2; // [2]
+  uint64_t* drain = bars + 2 * S + 5;    // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 6);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -182,7 +185,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t kTmemCols = 2 * BN;  // two accumulators; BN in {32, 64, 128}
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -236,17 +239,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_expect_tx(&full[stage], A_STAGE_BYTES);
           tma_load_2d(sA + stage * A_STAGE_BYTES, &tmap_x, &full[stage], kc * KCHUNK, static_cast<int>(mt * BM));
           ++issued;
-          if (++stage == STAGES) {
+          if (++stage == S) {
             stage = 0;
             phase ^= 1;
           }
         }
       }
-      // drain: the last min(issued, STAGES) copies must have landed before exit
-      const int64_t pending = std::min<int64_t>(issued, STAGES);
+      // drain: the last min(issued, S) copies must have landed before exit
+      const int64_t pending = std::min<int64_t>(issued, S);
       for (int64_t i = 0; i < pending; ++i) {
         if (--stage < 0) {
-          stage = STAGES - 1;
+          stage = S - 1;
           phase ^= 1;
         }
         if (!mbar_wait(&full[stage], phase)) record_timeout(5);
@@ -286,7 +289,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mma_tf32(d_tmem, a_desc, b_desc, idesc, (kc | kk) != 0 ? 1u : 0u);
           }
           mma_commit(&empty[stage]);
-          if (++stage == STAGES) {
+          if (++stage == S) {
             stage = 0;
             phase ^= 1;
           }
@@ -398,9 +401,26 @@ bool shape_ok(int64_t m, int64_t k, int64_t n) {
          n <= 65536;
 }
 
-size_t smem_bytes(int bn, int64_t k) {
+size_t smem_bytes_for(int bn, int64_t k, int stages) {
   const size_t w = ((static_cast<size_t>(bn) * k * 4) + 1023) & ~size_t(1023);
-  return 1024 /* alignment slack */ + w + STAGES * A_STAGE_BYTES + 256 /* barriers + TMEM slot */;
+  return 1024 /* alignment slack */ + w + static_cast<size_t>(stages) * A_STAGE_BYTES +
+         256 /* barriers + TMEM slot */;
+}
+
+// Ring depth: gemm.stages when set (and it fits), else as many stages as the
+// shared memory left beside the resident W slice holds, up to MAX_STAGES. More
+// stages keep more X bytes in flight per SM, which is what bounds this
+// HBM-bound transform. 0 when not even two stages fit.
+int stages_for(int bn, int64_t k) {
+  const int want = static_cast<int>(config().gemm_stages.load());
+  int s = want > 0 ? want : MAX_STAGES;
+  while (s >= 2 && smem_bytes_for(bn, k, s) > kSmemLimit) --s;
+  return s >= 2 ? s : 0;
+}
+
+size_t smem_bytes(int bn, int64_t k) {
+  const int s = stages_for(bn, k);
+  return s ? smem_bytes_for(bn, k, s) : kSmemLimit + 1;
 }
 
 template <int BN>
@@ -444,6 +464,8 @@ int launch_bn(const float* x, const float* w, const float* bias, float* out, int
   p.bias = bias;
   p.out = out;
   p.relu = relu ? 1 : 0;
+  p.stages = stages_for(BN, k);
+  if (p.stages < 2) return fail(GNN_ERR_UNSUPPORTED, "gemm_tf32_tc_kernel: shared memory too small for K");
   const int64_t tiles = p.m_tiles * p.n_tiles;
   int64_t ctas = std::min<int64_t>(tiles, sm_count());
   ctas = std::max<int64_t>(p.n_tiles, (ctas / p.n_tiles) * p.n_tiles);
@@ -459,7 +481,7 @@ bool gemm_tc_eligible(const float* x, const float* w, const float* bias, const f
   const uintptr_t a = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) |
                       reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(bias);
   return shape_ok(m, k, n) && (a % 16 == 0) && device_is_sm100() && encode_fn() != nullptr &&
-         smem_bytes(pick_bn(n), k) <= 227 * 1024;
+         smem_bytes(pick_bn(n), k) <= kSmemLimit;
 }
 
 int gemm_tc_tf32(const float* x, const float* w, const float* bias, float* out, int64_t m, int64_t k, int64_t n,
