@@ -84,6 +84,14 @@ extern "C" int gnn_config_set_int(const char* name, int64_t value) {
     GNN_REQUIRE(value == 0 || (value >= 2 && value <= 8), GNN_ERR_INVALID_ARGUMENT,
                 "gemm.stages must be 0 (automatic) or in [2, 8]");
     config().gemm_stages.store(value);
+  } else if (std::strcmp(name, "spmm.schedule") == 0) {
+    GNN_REQUIRE(value >= 0 && value <= 2, GNN_ERR_INVALID_ARGUMENT,
+                "spmm.schedule must be 0 (id order), 1 (windowed degree order) or 2 (global degree order)");
+    config().spmm_schedule.store(value);
+  } else if (std::strcmp(name, "spmm.schedule_window") == 0) {
+    GNN_REQUIRE(value >= 1024 && value <= (int64_t(1) << 30), GNN_ERR_INVALID_ARGUMENT,
+                "spmm.schedule_window must be in [1024, 2^30]");
+    config().spmm_schedule_window.store(value);
   } else {
     return fail(GNN_ERR_INVALID_ARGUMENT, std::string("unknown config key: ") + name);
   }
@@ -101,6 +109,10 @@ extern "C" int gnn_config_get_int(const char* name, int64_t* value) {
     *value = config().spmm_kernel.load();
   } else if (std::strcmp(name, "gemm.stages") == 0) {
     *value = config().gemm_stages.load();
+  } else if (std::strcmp(name, "spmm.schedule") == 0) {
+    *value = config().spmm_schedule.load();
+  } else if (std::strcmp(name, "spmm.schedule_window") == 0) {
+    *value = config().spmm_schedule_window.load();
   } else {
     return fail(GNN_ERR_INVALID_ARGUMENT, std::string("unknown config key: ") + name);
   }

@@ -972,24 +972,69 @@ __global__ void __launch_bounds__(1024) sched_scan_kernel(const uint32_t* __rest
   if (t == 1023) cursor[kDegBuckets] = part[t];  // the long-row class comes after all of them
 }
 
+// Global order, last step. Each block takes a contiguous chunk of rows, counts
+// its rows per class in shared memory, reserves one contiguous range per class
+// with a single global atomic, and places its rows inside its ranges (shared
+// atomics): global atomics scale with blocks x classes, not with rows.
 template <class IdxT>
 __global__ void __launch_bounds__(256) sched_scatter_kernel(const IdxT* __restrict__ rp, int64_t n, int64_t long_thr,
-                                                            uint32_t* __restrict__ cursor,
+                                                            int64_t chunk, uint32_t* __restrict__ cursor,
                                                             uint32_t* __restrict__ order) {
-  const int lane = threadIdx.x & 31;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t base = static_cast<int64_t>(blockIdx.x) * blockDim.x; base < n; base += stride) {
-    const int64_t r = base + threadIdx.x;
-    const bool live = r < n;
-    int bin = -1;
-    if (live) bin = sched_bin(static_cast<int64_t>(rp[r + 1]) - static_cast<int64_t>(rp[r]), long_thr);
-    // lanes of the same class share one atomic: the lowest lane reserves for the group
-    const unsigned group = __match_any_sync(0xffffffffu, bin);
-    const int leader = __ffs(group) - 1;
-    uint32_t first = 0;
-    if (live && lane == leader) first = atomicAdd(&cursor[bin], static_cast<uint32_t>(__popc(group)));
-    first = __shfl_sync(0xffffffffu, first, leader);
-    if (live) order[first + __popc(group & ((1u << lane) - 1u))] = static_cast<uint32_t>(r);
+  __shared__ uint32_t cnt[kSchedBins];
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * chunk;
+  const int64_t r1 = r0 + chunk < n ? r0 + chunk : n;
+  for (int i = threadIdx.x; i < kSchedBins; i += blockDim.x) cnt[i] = 0;
+  __syncthreads();
+  for (int64_t r = r0 + threadIdx.x; r < r1; r += blockDim.x) {
+    atomicAdd(&cnt[sched_bin(static_cast<int64_t>(rp[r + 1]) - static_cast<int64_t>(rp[r]), long_thr)], 1u);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < kSchedBins; i += blockDim.x) {
+    if (cnt[i]) cnt[i] = atomicAdd(&cursor[i], cnt[i]);  // this block's first position in class i
+  }
+  __syncthreads();
+  for (int64_t r = r0 + threadIdx.x; r < r1; r += blockDim.x) {
+    const int b = sched_bin(static_cast<int64_t>(rp[r + 1]) - static_cast<int64_t>(rp[r]), long_thr);
+    order[atomicAdd(&cnt[b], 1u)] = static_cast<uint32_t>(r);
+  }
+}
+
+// Windowed order: one block sorts one window of `window` consecutive rows by
+// class (highest degree first, the long-row kernel's rows last) into the same
+// window of the order. Rows keep their neighbourhood in id order — graphs
+// numbered by community keep their gather locality — while the rows that
+// share a block of the per-row kernel have about the same degree.
+template <class IdxT>
+__global__ void __launch_bounds__(1024) sched_window_kernel(const IdxT* __restrict__ rp, int64_t n, int64_t long_thr,
+                                                            int64_t window, uint32_t* __restrict__ order) {
+  __shared__ uint32_t cnt[kSchedBins];
+  __shared__ uint32_t part[1024];
+  const int t = threadIdx.x;
+  const int64_t w0 = static_cast<int64_t>(blockIdx.x) * window;
+  const int64_t w1 = w0 + window < n ? w0 + window : n;
+  for (int i = t; i < kSchedBins; i += blockDim.x) cnt[i] = 0;
+  __syncthreads();
+  for (int64_t r = w0 + t; r < w1; r += blockDim.x) {
+    atomicAdd(&cnt[sched_bin(static_cast<int64_t>(rp[r + 1]) - static_cast<int64_t>(rp[r]), long_thr)], 1u);
+  }
+  __syncthreads();
+  // exclusive prefix over degree classes in descending order; thread t owns class kDegBuckets-1-t
+  const uint32_t mine = cnt[kDegBuckets - 1 - t];
+  part[t] = mine;
+  __syncthreads();
+  for (int off = 1; off < 1024; off <<= 1) {
+    const uint32_t v = t >= off ? part[t - off] : 0u;
+    __syncthreads();
+    part[t] += v;
+    __syncthreads();
+  }
+  const uint32_t base = static_cast<uint32_t>(w0);
+  cnt[kDegBuckets - 1 - t] = base + part[t] - mine;
+  if (t == 1023) cnt[kDegBuckets] = base + part[t];
+  __syncthreads();
+  for (int64_t r = w0 + t; r < w1; r += blockDim.x) {
+    const int b = sched_bin(static_cast<int64_t>(rp[r + 1]) - static_cast<int64_t>(rp[r]), long_thr);
+    order[atomicAdd(&cnt[b], 1u)] = static_cast<uint32_t>(r);
   }
 }
 
@@ -1266,22 +1311,32 @@ int run_typed(const SpmmRequest& q, cudaStream_t stream) {
     a.long_thr = INT64_MAX;
   }
   // degree-ordered schedule for the per-row kernel, when the workspace holds it
-  if (q.sched == nullptr && config().spmm_kernel.load() == 1 && q.n >= kSchedMinRows && q.n <= UINT32_MAX &&
-      q.ws_bytes >= lay.total + sched_bytes(q.n)) {
+  const int64_t sched_mode = config().spmm_schedule.load();
+  if (q.sched == nullptr && sched_mode != 0 && config().spmm_kernel.load() == 1 && q.n >= kSchedMinRows &&
+      q.n <= UINT32_MAX && q.ws_bytes >= lay.total + sched_bytes(q.n)) {
     uint32_t* counts = reinterpret_cast<uint32_t*>(ws + lay.total);
     uint32_t* cursor = counts + kSchedBins;
     uint32_t* order = reinterpret_cast<uint32_t*>(ws + lay.total + ((2 * kSchedBins * sizeof(uint32_t) + 255) &
                                                                      ~size_t(255)));
-    GNN_CUDA_TRY(cudaMemsetAsync(counts, 0, kSchedBins * sizeof(uint32_t), stream), "spmm: schedule reset");
     const IdxT* rp = static_cast<const IdxT*>(q.row_ptr);
-    const int64_t want = (q.n + 255) / 256;
-    const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, 4LL * sm_count())));
-    sched_hist_kernel<IdxT><<<blocks, 256, 0, stream>>>(rp, q.n, a.long_thr, counts);
-    GNN_LAUNCH_CHECK("spmm schedule histogram");
-    sched_scan_kernel<<<1, 1024, 0, stream>>>(counts, cursor);
-    GNN_LAUNCH_CHECK("spmm schedule scan");
-    sched_scatter_kernel<IdxT><<<blocks, 256, 0, stream>>>(rp, q.n, a.long_thr, cursor, order);
-    GNN_LAUNCH_CHECK("spmm schedule scatter");
+    const int64_t window = config().spmm_schedule_window.load();
+    if (sched_mode == 1) {
+      const int64_t blocks = (q.n + window - 1) / window;
+      sched_window_kernel<IdxT><<<static_cast<unsigned>(blocks), 1024, 0, stream>>>(rp, q.n, a.long_thr, window,
+                                                                                    order);
+      GNN_LAUNCH_CHECK("spmm schedule (windowed)");
+    } else {
+      GNN_CUDA_TRY(cudaMemsetAsync(counts, 0, kSchedBins * sizeof(uint32_t), stream), "spmm: schedule reset");
+      const int64_t want = (q.n + 255) / 256;
+      const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, 4LL * sm_count())));
+      sched_hist_kernel<IdxT><<<blocks, 256, 0, stream>>>(rp, q.n, a.long_thr, counts);
+      GNN_LAUNCH_CHECK("spmm schedule histogram");
+      sched_scan_kernel<<<1, 1024, 0, stream>>>(counts, cursor);
+      GNN_LAUNCH_CHECK("spmm schedule scan");
+      const int64_t chunk = (q.n + blocks - 1) / blocks;
+      sched_scatter_kernel<IdxT><<<blocks, 256, 0, stream>>>(rp, q.n, a.long_thr, chunk, cursor, order);
+      GNN_LAUNCH_CHECK("spmm schedule scatter");
+    }
     a.sched32 = order;
   }
   return launch_vec<WM, MEAN, HOT, IdxT>(a, stream);

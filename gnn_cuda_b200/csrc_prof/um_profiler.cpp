@@ -18,6 +18,7 @@
 // library itself never depends on CUPTI.
 #include <cupti.h>
 #include <dlfcn.h>
+#include <unistd.h>
 
 #include <algorithm>
 #include <cstdint>
@@ -123,6 +124,14 @@ extern "C" int gnn_um_profiler_start(void) {
     g_error.clear();
     return GNN_OK;
   }
+  // The unified-memory counters come from the driver's UVM tools interface
+  // (/dev/nvidia-uvm-tools). Where that node is absent or closed (containers
+  // often do not map it) CUPTI's enable fails in several ways and was seen to
+  // crash the process, so it is not attempted at all.
+  if (access("/dev/nvidia-uvm-tools", R_OK | W_OK) != 0) {
+    return fail(GNN_ERR_UNSUPPORTED,
+                "unified-memory counters need /dev/nvidia-uvm-tools, which this system does not provide");
+  }
   const int drc = init_driver();
   if (drc != GNN_OK) return drc;
   CUptiResult r;
@@ -131,39 +140,21 @@ extern "C" int gnn_um_profiler_start(void) {
     if (r != CUPTI_SUCCESS) return cupti_fail(r, "cuptiActivityRegisterCallbacks");
     g_registered = true;
   }
-  // Not every counter kind exists on every platform (the driver rejects the
-  // enable with CUPTI_ERROR_INVALID_PARAMETER when one does not), so the kinds
-  // are tried from the full set down to the ones the migration report needs.
-  constexpr size_t nk = sizeof(kKinds) / sizeof(kKinds[0]);
-  const size_t tiers[] = {nk, 3 /* HtoD, DtoH, GPU faults */, 2 /* HtoD, DtoH */};
-  CUptiResult last = CUPTI_SUCCESS;
-  const CUpti_ActivityUnifiedMemoryCounterScope scopes[] = {
-      CUPTI_ACTIVITY_UNIFIED_MEMORY_COUNTER_SCOPE_PROCESS_SINGLE_DEVICE,
-      CUPTI_ACTIVITY_UNIFIED_MEMORY_COUNTER_SCOPE_PROCESS_ALL_DEVICES};
-  r = CUPTI_ERROR_UNKNOWN;
-  for (size_t want : tiers) {
-    for (CUpti_ActivityUnifiedMemoryCounterScope scope : scopes) {
-      CUpti_ActivityUnifiedMemoryCounterConfig cfg[nk];
-      std::memset(cfg, 0, sizeof(cfg));
-      for (size_t i = 0; i < nk; ++i) {
-        cfg[i].scope = scope;
-        cfg[i].kind = kKinds[i];
-        cfg[i].deviceId = 0;
-        cfg[i].enable = i < want ? 1 : 0;
-      }
-      r = cuptiActivityConfigureUnifiedMemoryCounter(cfg, static_cast<uint32_t>(nk));
-      if (r == CUPTI_SUCCESS) r = cuptiActivityEnable(CUPTI_ACTIVITY_KIND_UNIFIED_MEMORY_COUNTER);
-      if (r == CUPTI_SUCCESS) break;
-      last = r;
-      if (r == CUPTI_ERROR_UM_PROFILING_NOT_SUPPORTED || r == CUPTI_ERROR_UM_PROFILING_NOT_SUPPORTED_ON_DEVICE) {
-        return cupti_fail(r, "enabling CUPTI unified-memory counters");
-      }
-    }
-    if (r == CUPTI_SUCCESS) {
-      g_kinds = want;
-      break;
-    }
+  // One attempt with the three kinds the migration report needs; no retries
+  // with other settings after a failure.
+  constexpr size_t nk = 3;  // HtoD bytes, DtoH bytes, GPU page faults
+  CUpti_ActivityUnifiedMemoryCounterConfig cfg[nk];
+  std::memset(cfg, 0, sizeof(cfg));
+  for (size_t i = 0; i < nk; ++i) {
+    cfg[i].scope = CUPTI_ACTIVITY_UNIFIED_MEMORY_COUNTER_SCOPE_PROCESS_SINGLE_DEVICE;
+    cfg[i].kind = kKinds[i];
+    cfg[i].deviceId = 0;
+    cfg[i].enable = 1;
   }
+  r = cuptiActivityConfigureUnifiedMemoryCounter(cfg, static_cast<uint32_t>(nk));
+  if (r == CUPTI_SUCCESS) r = cuptiActivityEnable(CUPTI_ACTIVITY_KIND_UNIFIED_MEMORY_COUNTER);
+  const CUptiResult last = r;
+  if (r == CUPTI_SUCCESS) g_kinds = nk;
   if (r != CUPTI_SUCCESS) return cupti_fail(last, "enabling CUPTI unified-memory counters");
   g_enabled = true;
   g_error.clear();

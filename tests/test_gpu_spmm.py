@@ -363,7 +363,8 @@ def test_degree_schedule_matches_row_order_and_oracle(idx):
     assert big > small + n * 4 - 1
     it = N.GNN_INDEX_INT64 if idx == torch.int64 else N.GNN_INDEX_INT32
     stream = torch.cuda.current_stream(DEV).cuda_stream
-    old = [N.config_get(k) for k in ("spmm.kernel", "spmm.long_row_threshold", "spmm.long_row_warps")]
+    keys = ("spmm.kernel", "spmm.long_row_threshold", "spmm.long_row_warps", "spmm.schedule", "spmm.schedule_window")
+    old = [N.config_get(k) for k in keys]
     N.config_set("spmm.kernel", 1)
     N.config_set("spmm.long_row_threshold", 256)
     N.config_set("spmm.long_row_warps", 16)
@@ -371,7 +372,10 @@ def test_degree_schedule_matches_row_order_and_oracle(idx):
         for mode, exp in (("gcn", O.spmm(rp, ci, x, mode=O.W_GCN, dis=dis, split_warps=16, long_thr=256)),
                           ("sum", O.spmm(rp, ci, x, mode=O.W_UNIT, split_warps=16, long_thr=256))):
             outs = []
-            for nbytes in (small, big):
+            runs = [(small, 1, 4096), (big, 0, 4096), (big, 1, 4096), (big, 1, 1024), (big, 1, 1 << 20), (big, 2, 4096)]
+            for nbytes, sched, window in runs:
+                N.config_set("spmm.schedule", sched)
+                N.config_set("spmm.schedule_window", window)
                 ws = torch.empty(nbytes, dtype=torch.uint8, device=DEV)
                 o = torch.full((n, f), float("nan"), device=DEV)
                 if mode == "gcn":
@@ -384,8 +388,8 @@ def test_degree_schedule_matches_row_order_and_oracle(idx):
                                                 ctypes.c_void_p(stream))
                 N.check(rc)
                 outs.append(o.cpu().numpy())
-            for o in outs:
-                assert _bits_equal(o, exp), mode
+            for o, run in zip(outs, runs):
+                assert _bits_equal(o, exp), (mode, run)
     finally:
-        for k, v in zip(("spmm.kernel", "spmm.long_row_threshold", "spmm.long_row_warps"), old):
+        for k, v in zip(keys, old):
             N.config_set(k, v)

@@ -46,8 +46,8 @@ print(json.dumps(out))
 
 def test_um_counters_see_migrations_and_faults():
     res = subprocess.run([sys.executable, "-c", _TOUCH, str(ROOT)], capture_output=True, text=True, timeout=300)
-    if "UM_PROFILING_NOT_SUPPORTED" in res.stderr:
-        pytest.skip("CUPTI reports unified-memory profiling unsupported on this system")
+    if "UM_PROFILING_NOT_SUPPORTED" in res.stderr or "nvidia-uvm-tools" in res.stderr:
+        pytest.skip("unified-memory counters are not available on this system")
     assert res.returncode == 0, res.stderr[-3000:]
     out = json.loads(res.stdout.strip().splitlines()[-1])
     size = 64 * 2**20
@@ -90,8 +90,11 @@ def test_profile_spmm_migration_reports_feature_range_traffic(tmp_path, ft_matri
     vals = _summary(res.stdout)
     feature_bytes = n * 256 * 4
     assert vals["spmm_ns"] > 0
-    assert vals["HtoD_bytes"] >= 0.5 * feature_bytes  # the features are initialised on the host side
-    if prefetch == 0:
-        assert vals["GPU_faults"] > 0
+    if "nvidia-uvm-tools" in res.stderr:  # no counters on this system: the SpMM time is still reported
+        assert np.isnan(vals["HtoD_bytes"]) and np.isnan(vals["GPU_faults"])
+    else:
+        assert vals["HtoD_bytes"] >= 0.5 * feature_bytes  # the features are initialised on the host side
+        if prefetch == 0:
+            assert vals["GPU_faults"] > 0
     summaries = list((tmp_path / "out").glob("*_summary.txt"))
     assert len(summaries) == 1 and "HtoD_bytes" in summaries[0].read_text()
