@@ -185,6 +185,13 @@ def build_problem(seed: int, device: torch.device, scale: float):
     return dict(n=n, nnz=int(ci.numel()), rp=rp, ci=ci, dis=dis, x=x, ws=ws, bs=bs)
 
 
+def row_order() -> str:
+    """The per-row aggregation kernel's row order (spmm.schedule knob)."""
+    mode = N.config_get("spmm.schedule")
+    return {0: "row id", 1: f"degree-descending within windows of {N.config_get('spmm.schedule_window')} rows",
+            2: "degree-descending (global)"}[mode]
+
+
 def describe(prob, world: int, gemm: str | None = None, chunks: int = 1, exchange: str = "push",
              transport: str = "sm", layout: str = "balanced") -> dict:
     if gemm is None:
@@ -197,7 +204,7 @@ def describe(prob, world: int, gemm: str | None = None, chunks: int = 1, exchang
                                              f"+{layout}_halo_push_pieces{chunks}" if exchange == "halo" else
                                              f"+{layout}_nccl_allgather_pieces{chunks}"),
             "l2": "inputs larger than L2 (X is %.2f GB), no flush" % (prob["n"] * FEAT * 4 / 1e9),
-            "gemm": gemm}
+            "gemm": gemm, "row_order": row_order()}
 
 
 # ---------------------------------------------------------------------------
@@ -241,7 +248,7 @@ def run_ours(args, rank: int, world: int, device: torch.device):
     rows = shard.num_rows
     torch.backends.cuda.matmul.allow_tf32 = True  # the reference driver's --tf32 default
 
-    def step(timers=None):
+    def step(timers=None, final_out=None):
         if world == 1:
             # the reference-facing op surface, exactly what gcn_inference calls
             x = prob["x"]
@@ -250,12 +257,15 @@ def run_ours(args, rank: int, world: int, device: torch.device):
                 gcn_ops.spmm_gcn_forward_(prob["rp"], prob["ci"], prob["dis"], x, bufs["agg"])
                 partition._mark(timers, "spmm_end", ev)
                 out = bufs["out0" if li % 2 == 0 else "out1"]
+                if final_out is not None and li == LAYERS - 1:
+                    out = final_out
                 agg_ops.linear_forward_(bufs["agg"], prob["ws"][li], prob["bs"][li], out, li != LAYERS - 1)
                 x = out
             return x
         if args.exchange in ("push", "halo"):
             return partition.gcn_forward_push(shard, prob["dis"], prob["x"], prob["ws"], prob["bs"], layout, exchange,
-                                              bufs["agg"], bufs["out"], timers=timers, halo=halo)
+                                              bufs["agg"], bufs["out"] if final_out is None else final_out,
+                                              timers=timers, halo=halo)
         return partition.gcn_forward_allgather(shard, prob["dis"], prob["x"], prob["ws"], prob["bs"], layout, bufs,
                                                timers=timers)
 
@@ -287,28 +297,53 @@ def run_ours(args, rank: int, world: int, device: torch.device):
     # ---- e2e through the public API with host buffers ----
     # every step copies this rank's inputs (its CSR rows, the normalisation vector,
     # the full feature matrix, the weights) from pinned host memory, runs the
-    # forward and reads its output rows back into pinned host memory.
+    # forward and reads its output rows back into pinned host memory. The copies
+    # overlap across steps, as a serving loop would run them: step i+1's inputs
+    # go up on one copy stream while step i's output comes down on another (the
+    # PCIe link carries both directions at once); the forward of step i+1 waits
+    # for its inputs, and two output buffers alternate so that it never
+    # overwrites rows still being read back.
     if world == 1:
         dev_in = [prob["rp"], prob["ci"], prob["dis"], prob["x"]]
     else:
         dev_in = [t for p in shard.pieces for t in (p.row_ptr, p.col_ind) if t.numel()] + [prob["dis"], prob["x"]]
     dev_in += prob["ws"] + prob["bs"]
     host_in = [t.cpu().pin_memory() for t in dev_in]
-    out_host = torch.empty(rows, FEAT, pin_memory=True)
+    out_host = [torch.empty(rows, FEAT, pin_memory=True) for _ in range(2)]
     h2d = sum(t.numel() * t.element_size() for t in host_in)
-    d2h = out_host.numel() * 4
+    d2h = out_host[0].numel() * 4
+    pipelined = world == 1 or args.exchange in ("push", "halo")
+    if pipelined:
+        first = bufs["out1"] if world == 1 else bufs["out"]
+        out_dev = [first, torch.empty_like(first)]
+    else:
+        out_dev = [None, None]
+    comp = torch.cuda.current_stream(device)
+    s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    ev_out: list = [None, None]
     torch.cuda.synchronize(device)
     if world > 1:
         dist.barrier()
     e_start = torch.cuda.Event(enable_timing=True)
     e_end = torch.cuda.Event(enable_timing=True)
-    e_start.record()
-    for _ in range(args.e2e_steps):
-        for dst_t, src_t in zip(dev_in, host_in):
-            dst_t.copy_(src_t, non_blocking=True)
-        out = step()
-        out_host.copy_(out, non_blocking=True)
-    e_end.record()
+    e_start.record(comp)
+    for i in range(args.e2e_steps):
+        k = i % 2 if pipelined else 0
+        s_in.wait_stream(comp)  # the previous forward no longer reads the inputs
+        with torch.cuda.stream(s_in):
+            for dst_t, src_t in zip(dev_in, host_in):
+                dst_t.copy_(src_t, non_blocking=True)
+        comp.wait_stream(s_in)
+        if ev_out[k] is not None:
+            comp.wait_event(ev_out[k])  # the read-back that used this output buffer is done
+        out = step(final_out=out_dev[k])
+        s_out.wait_stream(comp)
+        with torch.cuda.stream(s_out):
+            out_host[k].copy_(out, non_blocking=True)
+            ev_out[k] = torch.cuda.Event()
+            ev_out[k].record(s_out)
+    comp.wait_stream(s_out)
+    e_end.record(comp)
     torch.cuda.synchronize(device)
     e2e_ms = e_start.elapsed_time(e_end)
 
@@ -355,6 +390,8 @@ def run_ours(args, rank: int, world: int, device: torch.device):
                      "spmm_ms_per_rank": [round(float(v), 4) for v in table[:, 2]]},
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h), "ms_per_step": round(e2e_ms / args.e2e_steps, 3),
+                "copies": "overlapped across steps (inputs up / output down on two copy streams)" if pipelined
+                else "in step order",
                 "api": "gnn_cuda_b200.GNN_cuda_common.gcn_ops/agg_ops over libgnnb200.so"},
         "gpu_launches": int(launches),
         "clocks": clocks.summary(),
@@ -540,7 +577,7 @@ def run_sage(args, device: torch.device) -> dict:
                                "linear, ReLU between layers)", "nodes": n, "csr_entries": nnz, "feat_dim": SAGE_FEAT,
                    "layers": LAYERS, "self_loops": False,
                    "gemm": "tcgen05-tf32" if N.lib().gnn_gemm_uses_tensor_cores(n, SAGE_FEAT, SAGE_FEAT)
-                   else "ffma-fp32",
+                   else "ffma-fp32", "row_order": row_order(),
                    "l2": "X is %.2f GB (reused ~%d times per layer), no flush" % (n * SAGE_FEAT * 4 / 1e9,
                                                                                  nnz // max(1, n))},
         "roofline": {"bound": "hbm", "kernel": "spmm_vec_kernel + spmm_long_kernel (mean aggregation)",
