@@ -189,7 +189,9 @@ def row_order() -> str:
     """The per-row aggregation kernel's row order (spmm.schedule knob)."""
     mode = N.config_get("spmm.schedule")
     return {0: "row id", 1: f"degree-descending within windows of {N.config_get('spmm.schedule_window')} rows",
-            2: "degree-descending (global)"}[mode]
+            2: "degree-descending (global)",
+            3: "degree-descending: global below 64 entries per row on average, else within windows of "
+               f"{N.config_get('spmm.schedule_window')} rows"}[mode]
 
 
 def describe(prob, world: int, gemm: str | None = None, chunks: int = 1, exchange: str = "push",

@@ -85,8 +85,9 @@ extern "C" int gnn_config_set_int(const char* name, int64_t value) {
                 "gemm.stages must be 0 (automatic) or in [2, 8]");
     config().gemm_stages.store(value);
   } else if (std::strcmp(name, "spmm.schedule") == 0) {
-    GNN_REQUIRE(value >= 0 && value <= 2, GNN_ERR_INVALID_ARGUMENT,
-                "spmm.schedule must be 0 (id order), 1 (windowed degree order) or 2 (global degree order)");
+    GNN_REQUIRE(value >= 0 && value <= 3, GNN_ERR_INVALID_ARGUMENT,
+                "spmm.schedule must be 0 (id order), 1 (windowed degree order), 2 (global degree order) or "
+                "3 (automatic)");
     config().spmm_schedule.store(value);
   } else if (std::strcmp(name, "spmm.schedule_window") == 0) {
     GNN_REQUIRE(value >= 1024 && value <= (int64_t(1) << 30), GNN_ERR_INVALID_ARGUMENT,

@@ -57,8 +57,10 @@ struct Config {
   std::atomic<int64_t> long_row_warps{16};
   std::atomic<int64_t> spmm_kernel{1};  // 0 packed stream, 1 one warp per row (default), 2 cp.async staging
   std::atomic<int64_t> gemm_stages{0};  // tcgen05 GEMM X-tile ring depth; 0 = as deep as shared memory allows
-  std::atomic<int64_t> spmm_schedule{1};         // per-row kernel row order: 0 id order, 1 windowed degree, 2 global degree
-  std::atomic<int64_t> spmm_schedule_window{4096};  // rows per window of the windowed degree order
+  // per-row kernel row order: 0 id order, 1 windowed degree, 2 global degree, 3 automatic (global below
+  // a mean degree of 64 entries per row, windowed above)
+  std::atomic<int64_t> spmm_schedule{3};
+  std::atomic<int64_t> spmm_schedule_window{2048};  // rows per window of the windowed degree order
 };
 Config& config();
 

@@ -69,7 +69,11 @@ const char* gnn_status_string(int status);
 /* Tuning knobs (process-wide). Names: "spmm.long_row_threshold" (edges; 0 =
  * automatic), "spmm.long_row_warps" (4..16), "spmm.kernel" (0 = persistent
  * packed-stream kernel; 1 = one warp per row, the default; 2 = packed stream
- * with cp.async staging through shared memory; all give identical results).
+ * with cp.async staging through shared memory; all give identical results),
+ * "spmm.schedule" (row order of the per-row kernel when the workspace holds a
+ * schedule: 0 id order, 1 degree order within windows of "spmm.schedule_window"
+ * rows, 2 global degree order, 3 automatic = 2 below a mean degree of 64 else 1;
+ * identical results), "gemm.stages" (tcgen05 GEMM ring depth, 0 = automatic).
  * Returns GNN_ERR_INVALID_ARGUMENT
  * for an unknown name or out-of-range value. */
 int gnn_config_set_int(const char* name, int64_t value);
