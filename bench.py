@@ -250,18 +250,19 @@ def run_ours(args, rank: int, world: int, device: torch.device):
     rows = shard.num_rows
     torch.backends.cuda.matmul.allow_tf32 = True  # the reference driver's --tf32 default
 
-    def step(timers=None, final_out=None):
+    def step(timers=None, final_out=None, inputs=None):
         if world == 1:
             # the reference-facing op surface, exactly what gcn_inference calls
-            x = prob["x"]
+            p = prob if inputs is None else inputs
+            x = p["x"]
             for li in range(LAYERS):
                 ev = partition._mark(timers, "spmm_begin")
-                gcn_ops.spmm_gcn_forward_(prob["rp"], prob["ci"], prob["dis"], x, bufs["agg"])
+                gcn_ops.spmm_gcn_forward_(p["rp"], p["ci"], p["dis"], x, bufs["agg"])
                 partition._mark(timers, "spmm_end", ev)
                 out = bufs["out0" if li % 2 == 0 else "out1"]
                 if final_out is not None and li == LAYERS - 1:
                     out = final_out
-                agg_ops.linear_forward_(bufs["agg"], prob["ws"][li], prob["bs"][li], out, li != LAYERS - 1)
+                agg_ops.linear_forward_(bufs["agg"], p["ws"][li], p["bs"][li], out, li != LAYERS - 1)
                 x = out
             return x
         if args.exchange in ("push", "halo"):
@@ -304,13 +305,21 @@ def run_ours(args, rank: int, world: int, device: torch.device):
     # go up on one copy stream while step i's output comes down on another (the
     # PCIe link carries both directions at once); the forward of step i+1 waits
     # for its inputs, and two output buffers alternate so that it never
-    # overwrites rows still being read back.
+    # overwrites rows still being read back. On one GPU two input sets alternate
+    # as well, so the upload of step i+1 also overlaps the forward of step i.
     if world == 1:
         dev_in = [prob["rp"], prob["ci"], prob["dis"], prob["x"]]
     else:
         dev_in = [t for p in shard.pieces for t in (p.row_ptr, p.col_ind) if t.numel()] + [prob["dis"], prob["x"]]
     dev_in += prob["ws"] + prob["bs"]
     host_in = [t.cpu().pin_memory() for t in dev_in]
+    in_sets = [dev_in]
+    if world == 1:
+        in_sets.append([torch.empty_like(t) for t in dev_in])
+
+    def as_inputs(ts):
+        return {"rp": ts[0], "ci": ts[1], "dis": ts[2], "x": ts[3], "ws": ts[4:4 + LAYERS],
+                "bs": ts[4 + LAYERS:4 + 2 * LAYERS]}
     out_host = [torch.empty(rows, FEAT, pin_memory=True) for _ in range(2)]
     h2d = sum(t.numel() * t.element_size() for t in host_in)
     d2h = out_host[0].numel() * 4
@@ -323,6 +332,7 @@ def run_ours(args, rank: int, world: int, device: torch.device):
     comp = torch.cuda.current_stream(device)
     s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
     ev_out: list = [None, None]
+    ev_used: list = [None, None]  # the forward that last read input set j is done
     torch.cuda.synchronize(device)
     if world > 1:
         dist.barrier()
@@ -331,14 +341,20 @@ def run_ours(args, rank: int, world: int, device: torch.device):
     e_start.record(comp)
     for i in range(args.e2e_steps):
         k = i % 2 if pipelined else 0
-        s_in.wait_stream(comp)  # the previous forward no longer reads the inputs
+        j = i % len(in_sets)
+        if len(in_sets) == 1:
+            s_in.wait_stream(comp)  # the previous forward no longer reads the inputs
+        elif ev_used[j] is not None:
+            s_in.wait_event(ev_used[j])  # the forward two steps back is done with this input set
         with torch.cuda.stream(s_in):
-            for dst_t, src_t in zip(dev_in, host_in):
+            for dst_t, src_t in zip(in_sets[j], host_in):
                 dst_t.copy_(src_t, non_blocking=True)
         comp.wait_stream(s_in)
         if ev_out[k] is not None:
             comp.wait_event(ev_out[k])  # the read-back that used this output buffer is done
-        out = step(final_out=out_dev[k])
+        out = step(final_out=out_dev[k], inputs=as_inputs(in_sets[j]) if world == 1 else None)
+        ev_used[j] = torch.cuda.Event()
+        ev_used[j].record(comp)
         s_out.wait_stream(comp)
         with torch.cuda.stream(s_out):
             out_host[k].copy_(out, non_blocking=True)
@@ -392,7 +408,9 @@ def run_ours(args, rank: int, world: int, device: torch.device):
                      "spmm_ms_per_rank": [round(float(v), 4) for v in table[:, 2]]},
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h), "ms_per_step": round(e2e_ms / args.e2e_steps, 3),
-                "copies": "overlapped across steps (inputs up / output down on two copy streams)" if pipelined
+                "copies": ("overlapped across steps (two input sets and two output buffers; inputs up / output "
+                           "down on two copy streams beside the forward)" if world == 1 else
+                           "overlapped across steps (inputs up / output down on two copy streams)") if pipelined
                 else "in step order",
                 "api": "gnn_cuda_b200.GNN_cuda_common.gcn_ops/agg_ops over libgnnb200.so"},
         "gpu_launches": int(launches),
