@@ -390,7 +390,7 @@ def run_ours(args, rank: int, world: int, device: torch.device):
         return None
     peak, peak_kind = measured_hbm_gbs()
     achieved = shard_bytes / (spmm_ms_avg * 1e-3) / 1e9 if spmm_ms_avg > 0 else None
-    traffic = profiled_traffic()
+    traffic = profiled_traffic() if world == 1 and args.scale == 1.0 else None
     result = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "ms_per_layer": round(ms_step / LAYERS, 4),

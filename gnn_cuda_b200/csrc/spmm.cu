@@ -80,7 +80,10 @@ constexpr uint32_t kSegTag = 0x80000000u;
 #define GNN_SPMM_U_NV34 2
 #endif
 #ifndef GNN_SPMM_MIN_BLOCKS
-#define GNN_SPMM_MIN_BLOCKS 3  // at F <= 128 (one float4 per lane); wider rows keep 2
+// at F <= 128 (one float4 per lane); wider rows keep 2. Measured on B200 with the
+// degree-ordered rows: 4 blocks (32 registers) 3.06 ms vs 3 blocks (40) 3.26 ms per
+// aggregation of the products-shaped graph.
+#define GNN_SPMM_MIN_BLOCKS 4
 #endif
 // Long-row kernel (spmm_long_kernel): register budget, grid and gather depth.
 // Measured on B200 (products-shaped graph, F = 128): 64 registers and one
@@ -132,6 +135,7 @@ struct SpmmArgs {
   int64_t seg_len;          // entries per segment (long_split * kSegEdgesPerWarp)
   int tiles;                // feature tiles (grid.y)
   int long_split;           // warps per segment (spmm.long_row_warps)
+  int rows_per_warp;        // per-row kernel: rows a warp takes per block (2 or 4)
 };
 
 // Set by a segment whose bounded wait for its predecessor ran out (the row is
@@ -434,11 +438,15 @@ __global__ void __launch_bounds__(kBlockThreads, GNN_SPMM_LONG_MIN_BLOCKS)
   long_rows_phase<WM, MEAN, HOT, NV, IdxT>(a, s_part, &s_ticket);
 }
 
-// Per-row vector kernel: kRowsPerWarp rows per warp, skipping long rows
-// (spmm_long_kernel's).
-template <int WM, int MEAN, bool HOT, int NV, class IdxT>
+// Per-row vector kernel: RPW rows per warp, skipping long rows
+// (spmm_long_kernel's). RPW = 4 by default; 2 for dense graphs (mean degree of
+// 64 entries and more), where a warp's rows are long enough that fewer rows per
+// warp and more warps per row set win (measured on B200, Reddit-shaped graph:
+// 5.77 vs 6.33 ms per aggregation; products shape: 3.40 vs 3.26 ms the other way).
+template <int WM, int MEAN, bool HOT, int NV, class IdxT, int RPW>
 __global__ void __launch_bounds__(kBlockThreads, resident_blocks<NV>())
     spmm_vec_kernel(GNN_KPARAM SpmmArgs a) {
+  constexpr int kRowsPerWarp = RPW;
   constexpr int U = gather_depth<NV>();
 
   const int lane = threadIdx.x & 31;
@@ -1104,7 +1112,8 @@ int launch_vec(SpmmArgs a, cudaStream_t stream) {
   const int nv = static_cast<int>((lanes_f4 + 31) / 32);
   const int nwarps = static_cast<int>(config().long_row_warps.load());
   const int threads = nwarps * 32;
-  const int64_t rows_per_block = static_cast<int64_t>(nwarps) * kRowsPerWarp;
+  const int rpw = a.rows_per_warp == 2 ? 2 : kRowsPerWarp;
+  const int64_t rows_per_block = static_cast<int64_t>(nwarps) * (config().spmm_kernel.load() == 1 ? rpw : kRowsPerWarp);
   const int64_t normal_blocks = (a.n + rows_per_block - 1) / rows_per_block;
 
   const size_t smem = static_cast<size_t>(nwarps) * 32 * nv * sizeof(float4);
@@ -1151,7 +1160,11 @@ int launch_vec(SpmmArgs a, cudaStream_t stream) {
     int rc = GNN_OK;
     if (gx > 0) {
       dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(tiles));
-#define GNN_LAUNCH_NV(NVV) spmm_vec_kernel<WM, MEAN, HOT, NVV, IdxT><<<grid, block, 0, stream>>>(a)
+#define GNN_LAUNCH_NV(NVV)                                                          \
+  do {                                                                              \
+    if (rpw == 2) spmm_vec_kernel<WM, MEAN, HOT, NVV, IdxT, 2><<<grid, block, 0, stream>>>(a); \
+    else spmm_vec_kernel<WM, MEAN, HOT, NVV, IdxT, kRowsPerWarp><<<grid, block, 0, stream>>>(a); \
+  } while (0)
       switch (nv) {
         case 1: GNN_LAUNCH_NV(1); break;
         case 2: GNN_LAUNCH_NV(2); break;
@@ -1286,6 +1299,7 @@ int run_typed(const SpmmRequest& q, cudaStream_t stream) {
   a.long_cap = std::min<int64_t>(long_capacity(q.n, q.nnz), q.nnz / (a.long_thr + 1) + 1);
   a.long_split = static_cast<int>(config().long_row_warps.load());
   a.seg_len = static_cast<int64_t>(a.long_split) * kSegEdgesPerWarp;
+  a.rows_per_warp = q.nnz >= 64 * q.n ? 2 : kRowsPerWarp;
   a.tiles = static_cast<int>(tiles);
   if (q.nnz <= a.long_thr) a.long_cap = 0;  // no row can be long
   // the workspace holds the work tickets (and the long-row lists when needed)

@@ -393,3 +393,32 @@ def test_degree_schedule_matches_row_order_and_oracle(idx):
     finally:
         for k, v in zip(keys, old):
             N.config_set(k, v)
+
+
+@pytest.mark.parametrize("f", [128, 256])
+def test_dense_graph_two_rows_per_warp(f):
+    """Graphs with 64 or more entries per row on average take the per-row kernel
+    with two rows per warp and the windowed degree order: still bit-exact."""
+    n = 70_000
+    u, v = synth.community_lognormal(n, n * 40, seed=41)
+    s, d = synth.symmetrize(u, v)
+    rp, ci, dis = O.gcn_normalized_csr(s.numpy(), d.numpy(), n)
+    assert ci.size >= 64 * n
+    x = synth.features(n, f, seed=42).numpy()
+    t = {k: torch.from_numpy(a).to(DEV) for k, a in dict(rp=rp, ci=ci, dis=dis, x=x).items()}
+    keys = ("spmm.kernel", "spmm.long_row_threshold", "spmm.long_row_warps", "spmm.schedule")
+    old = [N.config_get(k) for k in keys]
+    for k, v in zip(keys, (1, 1024, 16, 3)):
+        N.config_set(k, v)
+    try:
+        exp_gcn = O.spmm(rp, ci, x, mode=O.W_GCN, dis=dis, split_warps=16, long_thr=1024)
+        exp_mean = O.spmm(rp, ci, x, mode=O.W_UNIT, mean=O.M_DIV, split_warps=16, long_thr=1024)
+        o = torch.full((n, f), float("nan"), device=DEV)
+        gcn_ops.spmm_gcn_forward_(t["rp"], t["ci"], t["dis"], t["x"], o)
+        assert _bits_equal(o.cpu().numpy(), exp_gcn)
+        o2 = torch.full((n, f), float("nan"), device=DEV)
+        agg_ops.spmm_mean_forward_(t["rp"], t["ci"], t["x"], o2)
+        assert _bits_equal(o2.cpu().numpy(), exp_mean)
+    finally:
+        for k, v in zip(keys, old):
+            N.config_set(k, v)
