@@ -76,7 +76,8 @@ def parse_args():
     ap.add_argument("--push-ctas", type=int, default=0, help="grid of the SM push kernel (0: 4 per SM)")
     ap.add_argument("--layout", choices=["balanced", "contiguous"], default="balanced",
                     help="N > 1: rows dealt to ranks by cost, or contiguous cost-balanced ranges")
-    ap.add_argument("--workload", choices=["gcn_products_like", "sage_reddit_like", "locality_products_like"],
+    ap.add_argument("--workload", choices=["gcn_products_like", "sage_reddit_like", "gin_papers_like",
+                                           "locality_products_like"],
                     default="gcn_products_like",
                     help="the GCN forward (default); the GraphSAGE-mean forward on the Reddit-shaped graph (1 GPU); "
                          "or the UVM locality preprocessing of the products-shaped graph (1 GPU)")
@@ -614,6 +615,92 @@ def run_sage(args, device: torch.device) -> dict:
 
 
 # ---------------------------------------------------------------------------
+# GIN workload (papers100M-shaped R-MAT graph, 3 layers, MLP 128-128-128)
+# ---------------------------------------------------------------------------
+
+GIN_FEAT, GIN_LAYERS = 128, 3
+
+
+def run_gin(args, device: torch.device) -> dict:
+    """gin_inference.py's layer, per layer: sum aggregation, + (1 + eps)·x (eps = 0),
+    Linear(128,128)+ReLU, Linear(128,128) (+ReLU between layers) — the reference's
+    composition (gin_inference.py:317-359) on this library's kernels. The whole
+    111M-node, 1.6B-entry graph needs X, the aggregate, the hidden and the output
+    matrices (4 x 57 GB) at once, more than one GPU holds; --scale picks the
+    fraction of nodes and entries (default 1/4 for this workload)."""
+    scale = args.scale if args.scale != 1.0 else 0.25
+    t0 = time.time()
+    src, dst, n = synth.make_graph("gin_papers_like", seed=args.seed, device=device, scale_nodes=scale)
+    nnz_est = int(src.numel())
+    rp, ci, _ = synth.csr_on_device(src, dst, n, add_self_loops=False,
+                                    index_dtype=torch.int64 if nnz_est > 2**31 - 1 else torch.int32)
+    del src, dst
+    torch.cuda.empty_cache()
+    nnz = int(ci.numel())
+    x = synth.features(n, GIN_FEAT, seed=args.seed + 1, device=device)
+    w1 = [synth.glorot(GIN_FEAT, GIN_FEAT, seed=args.seed + 10 + i, device=device) for i in range(GIN_LAYERS)]
+    w2 = [synth.glorot(GIN_FEAT, GIN_FEAT, seed=args.seed + 20 + i, device=device) for i in range(GIN_LAYERS)]
+    b = [torch.zeros(GIN_FEAT, device=device) for _ in range(GIN_LAYERS)]
+    agg = torch.empty(n, GIN_FEAT, device=device)
+    hid = torch.empty(n, GIN_FEAT, device=device)
+    outs = [torch.empty(n, GIN_FEAT, device=device) for _ in range(2)]
+    torch.cuda.synchronize(device)
+    log(f"[bench] gin graph n={n} nnz={nnz} built in {time.time() - t0:.1f}s")
+    torch.backends.cuda.matmul.allow_tf32 = True
+    timers: dict = {}
+
+    def step(tm=None):
+        h = x
+        for li in range(GIN_LAYERS):
+            ev = partition._mark(tm, "spmm_begin")
+            agg_ops.spmm_sum_forward_(rp, ci, h, agg)
+            partition._mark(tm, "spmm_end", ev)
+            agg_ops.tensor_add_inplace_(agg, h, 1.0)  # (1 + eps) * x with eps = 0
+            agg_ops.linear_forward_(agg, w1[li], b[li], hid, True)
+            o = outs[li % 2]
+            agg_ops.linear_forward_(hid, w2[li], b[li], o, li != GIN_LAYERS - 1)
+            h = o
+        return h
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(device)
+    launches0 = N.lib().gnn_kernel_launches()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device.index) as clocks:
+        e0.record()
+        for _ in range(args.steps):
+            step(timers)
+        e1.record()
+        torch.cuda.synchronize(device)
+    launches = N.lib().gnn_kernel_launches() - launches0
+    ms_step = e0.elapsed_time(e1) / args.steps
+    spmm_ms = sum(bb.elapsed_time(ee) for bb, ee in timers["spmm"]) / (args.steps * GIN_LAYERS)
+    bytes_layer = mean_layer_bytes(n, nnz, GIN_FEAT) + (rp.element_size() - 4) * (n + 1)
+    peak, peak_kind = measured_hbm_gbs()
+    achieved = bytes_layer / (spmm_ms * 1e-3) / 1e9
+    return {
+        "metric": METRIC, "value": round(bytes_layer * GIN_LAYERS / (ms_step * 1e-3) / 1e9, 2), "unit": "GB/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+        "ms_per_layer": round(ms_step / GIN_LAYERS, 4), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "fp32",
+        "data": f"synthetic: seeded R-MAT graph (seed {args.seed}) with the ogbn-papers100M shape at {scale:g} of its "
+                "nodes and entries, N(0,1) features, Glorot weights, zero bias",
+        "config": {"workload": f"gin_papers_like x{scale:g}: GIN 3 layers, eps = 0, MLP Linear(128,128)-ReLU-"
+                               "Linear(128,128), ReLU between layers", "nodes": n, "csr_entries": nnz,
+                   "feat_dim": GIN_FEAT, "layers": GIN_LAYERS, "self_loops": False,
+                   "row_ptr": "int64" if rp.dtype == torch.int64 else "int32", "row_order": row_order(),
+                   "l2": "inputs larger than L2 (X is %.1f GB), no flush" % (n * GIN_FEAT * 4 / 1e9)},
+        "roofline": {"bound": "hbm", "kernel": "spmm_vec_kernel + spmm_long_kernel (sum aggregation)",
+                     "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                     "peak_source": peak_kind, "spmm_ms_per_layer": round(spmm_ms, 4),
+                     "algorithmic_bytes_per_layer": bytes_layer, "traffic": None},
+        "gpu_launches": int(launches), "clocks": clocks.summary(),
+    }
+
+
+# ---------------------------------------------------------------------------
 # locality preprocessing workload (the input of spmm_mode=optimized)
 # ---------------------------------------------------------------------------
 
@@ -696,6 +783,15 @@ def main() -> int:
         log(f"[bench] WORLD_SIZE={world} but --gpus={args.gpus}; using WORLD_SIZE")
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
+    if args.workload == "gin_papers_like":
+        if rank != 0:
+            return 0
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the CPU reference arm is measured on the "
+                              "default workload (gcn_products_like)"}), flush=True)
+        else:
+            print(json.dumps(run_gin(args, device)), flush=True)
+        return 0
     if args.workload == "sage_reddit_like":
         if rank != 0:
             return 0

@@ -194,6 +194,7 @@ WORKLOADS = {
     "gcn_pubmed_like": dict(n=19_717, pairs=44_324, gen="chung_lu", f=128, layers=1, model="gcn", loops=True),
     "gcn_products_like": dict(n=2_449_029, pairs=30_929_570, gen="rmat", f=128, layers=2, model="gcn", loops=True),
     "sage_reddit_like": dict(n=232_965, pairs=57_307_946, gen="community", f=256, layers=2, model="sage", loops=False),
+    "gin_papers_like": dict(n=111_059_956, pairs=807_842_936, gen="rmat", f=128, layers=3, model="gin", loops=False),
 }
 
 
