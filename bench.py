@@ -68,7 +68,7 @@ def parse_args():
     ap.add_argument("--scale", type=float, default=1.0, help="scale the graph down (smoke runs only)")
     ap.add_argument("--chunks", type=int, default=0,
                     help="row pieces per rank, exchanged as they finish (N > 1; 0: 2 from 8 GPUs up, else 1)")
-    ap.add_argument("--exchange", choices=["push", "halo", "allgather"], default="push",
+    ap.add_argument("--exchange", choices=["push", "halo", "allgather"], default="halo",
                     help="N > 1: pushes of whole row pieces into the peers' IPC-mapped buffers, pushes of only "
                          "the rows each peer reads (halo), or NCCL all_gather")
     ap.add_argument("--transport", choices=["sm", "ce"], default="sm",
@@ -195,7 +195,7 @@ def row_order() -> str:
                f"{N.config_get('spmm.schedule_window')} rows"}[mode]
 
 
-def describe(prob, world: int, gemm: str | None = None, chunks: int = 1, exchange: str = "push",
+def describe(prob, world: int, gemm: str | None = None, chunks: int = 1, exchange: str = "halo",
              transport: str = "sm", layout: str = "balanced") -> dict:
     if gemm is None:
         gemm = "tcgen05-tf32" if N.lib().gnn_gemm_uses_tensor_cores(prob["n"], FEAT, FEAT) else "ffma-fp32"
