@@ -526,23 +526,11 @@ __global__ void __launch_bounds__(kBlockThreads, resident_blocks<NV>())
     float4 acc[NV];
 #pragma unroll
     for (int q = 0; q < NV; ++q) acc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
-    // GIN's self term: its row is loaded before the gathers, so the load's
-    // latency hides behind them instead of delaying the store
-    float4 self[NV];
-    if constexpr (MEAN == kSelfAdd) {
-      const float4* xr = reinterpret_cast<const float4*>(a.self_x + r * a.f);
-#pragma unroll
-      for (int q = 0; q < NV; ++q) self[q] = valid[q] ? ldg_f4(xr + col0 + 32 * q) : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
     accumulate_edges<WM, HOT, NV, U, IdxT>(a, beg, end, rs, lane, col0, valid, acc, true, c_cur, w_cur);
     float4* orow = reinterpret_cast<float4*>(a.out + r * a.f);
 #pragma unroll
     for (int q = 0; q < NV; ++q) {
-      if constexpr (MEAN == kSelfAdd) {
-        if (valid[q]) orow[col0 + 32 * q] = fma4(a.self_alpha, self[q], acc[q]);
-      } else {
-        if (valid[q]) orow[col0 + 32 * q] = finish<MEAN>(acc[q], deg);
-      }
+      if (valid[q]) orow[col0 + 32 * q] = finish_row<MEAN>(a, acc[q], deg, r, col0 + 32 * q);
     }
   }
 }

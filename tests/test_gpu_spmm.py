@@ -431,7 +431,7 @@ def test_sum_self_matches_sum_then_add(f, idx):
     long rows split into segments (F = 31 takes the scalar path)."""
     n = 80_000
     s, d = _hub_graph(n, [20_000, 9_000], extra=200_000, seed=51)
-    rp, ci = O.plain_csr(s.numpy(), d.numpy(), n, add_self_loops=False)
+    rp, ci, _ = O.plain_csr(s.numpy(), d.numpy(), n, add_self_loops=False)
     x = synth.features(n, f, seed=52).to(DEV)
     t_rp = torch.from_numpy(rp).to(DEV).to(idx)
     t_ci = torch.from_numpy(ci).to(DEV)
