@@ -13,15 +13,6 @@ def spmm_sum_forward_(row_ptr: torch.Tensor, col_ind: torch.Tensor, x: torch.Ten
     (mod.spmm_sum_hmm_forward_ if hmm_optimized else mod.spmm_sum_forward_)(row_ptr, col_ind, x, out)
 
 
-def spmm_sum_self_forward_(row_ptr: torch.Tensor, col_ind: torch.Tensor, x: torch.Tensor, out: torch.Tensor,
-                           alpha: float = 1.0) -> None:
-    """GIN's aggregation in one pass: spmm_sum_forward_(row_ptr, col_ind, x, out) followed by
-    tensor_add_inplace_(out, x, alpha), with the same bits and one pass over out less. An
-    addition of this engine; the reference runs the two ops (gin_inference.py)."""
-    from . import native_ops
-    native_ops.spmm_sum_self_forward_(row_ptr, col_ind, x, out, float(alpha))
-
-
 def spmm_mean_forward_(row_ptr: torch.Tensor, col_ind: torch.Tensor, x: torch.Tensor, out: torch.Tensor, *,
                        hmm_optimized: bool = False) -> None:
     """hmm_optimized selects the reciprocal-multiply mean of the reference's hmm kernel."""

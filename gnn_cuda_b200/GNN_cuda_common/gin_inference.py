@@ -3,7 +3,6 @@
 Per layer (GINConv with an MLP Linear-ReLU-Linear):
     agg    = sum_{j in N(i)} x_j                 (spmm_sum_forward_)
     agg   += (1 + eps) * x                       (tensor_add_inplace_)
-                  (both in one pass here: spmm_sum_self_forward_, same bits)
     hidden = relu(agg·W1 + b1)                   (linear_forward_, tcgen05 GEMM)
     out    = hidden·W2 + b2, ReLU when post_layer_relu and not the last layer
 Same flags, placement and report as the reference. eps is read once per layer
@@ -19,7 +18,7 @@ from typing import Callable
 import torch
 
 from . import _driver as D
-from .agg_ops import linear_forward_, spmm_sum_self_forward_
+from .agg_ops import linear_forward_, spmm_sum_forward_, tensor_add_inplace_
 from .allocator import (
     ManagedAllocationConfig,
     allocate_empty,
@@ -141,10 +140,10 @@ def run_gin_inference(*, framework_label: str, select_device: Callable[[str], to
             tag = f"layer{idx + 1}"
             with D.nvtx_range(nvtx, f"{tag}/aggregation"):
                 with phases.measure("spmm"):
-                    # sum aggregation and the (1 + eps) * x self term in one pass: the same
-                    # bits as spmm_sum_forward_ followed by tensor_add_inplace_ (the reference's
-                    # two calls), one read and one write of [N, F] less
-                    spmm_sum_self_forward_(row_ptr, col_ind, x, layer.agg_buffer, alpha=layer.alpha)
+                    spmm_sum_forward_(row_ptr, col_ind, x, layer.agg_buffer, hmm_optimized=use_hmm_spmm)
+            with D.nvtx_range(nvtx, f"{tag}/epilogue"):
+                with phases.measure("epilogue"):
+                    tensor_add_inplace_(layer.agg_buffer, x, alpha=layer.alpha)
             with D.nvtx_range(nvtx, f"{tag}/dense_update"):
                 with phases.measure("gemm"):
                     linear_forward_(layer.agg_buffer, layer.weight1, layer.bias1, layer.hidden_buffer, True)

@@ -136,8 +136,6 @@ def _spmm_call(fn_name: str, row_ptr, col_ind, vec, x, out, *extra_args, optimiz
                     out.data_ptr(), n, nnz, f, ws, wsb, s)
         elif vec is None and fn_name == "gnn_spmm_mean_forward":
             rc = fn(rp, _index_type(row_ptr), ci, xp, out.data_ptr(), n, nnz, f, *extra_args, ws, wsb, s)
-        elif vec is None and fn_name == "gnn_spmm_sum_self_forward":
-            rc = fn(rp, _index_type(row_ptr), ci, xp, *extra_args, out.data_ptr(), n, nnz, f, ws, wsb, s)
         elif vec is None:
             rc = fn(rp, _index_type(row_ptr), ci, xp, out.data_ptr(), n, nnz, f, ws, wsb, s)
         else:
@@ -260,13 +258,6 @@ def spmm_sum_forward_(row_ptr, col_ind, x, out):
     """agg_ops.cu:315."""
     _check_csr_common(row_ptr, col_ind, x, out, {})
     _spmm_call("gnn_spmm_sum_forward", row_ptr, col_ind, None, x, out)
-
-
-def spmm_sum_self_forward_(row_ptr, col_ind, x, out, alpha=1.0):
-    """spmm_sum_forward_ then tensor_add_inplace_(out, x, alpha) (agg_ops.cu:315, :399) in one pass."""
-    _check_csr_common(row_ptr, col_ind, x, out, {})
-    _check(out.data_ptr() != x.data_ptr(), "out must not alias x")
-    _spmm_call("gnn_spmm_sum_self_forward", row_ptr, col_ind, None, x, out, ctypes.c_float(float(alpha)))
 
 
 def spmm_sum_hmm_forward_(row_ptr, col_ind, x, out):

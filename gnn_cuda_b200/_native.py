@@ -62,7 +62,6 @@ PROTOTYPES: dict[str, tuple[object, list[object]]] = {
     "gnn_spmm_pyg_gcn_optimized_forward": (
         _i32, [_vp, _i32, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _vp, _sz, _vp]),
     "gnn_spmm_sum_forward": (_i32, [_vp, _i32, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _sz, _vp]),
-    "gnn_spmm_sum_self_forward": (_i32, [_vp, _i32, _vp, _vp, _f32, _vp, _i64, _i64, _i64, _vp, _sz, _vp]),
     "gnn_spmm_mean_forward": (_i32, [_vp, _i32, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _vp, _sz, _vp]),
     "gnn_gemm_forward": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i32, _vp]),
     "gnn_linear_forward": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _i32, _vp]),

@@ -107,10 +107,7 @@ __host__ __device__ constexpr int resident_blocks() {
 }
 
 enum WeightMode : int { kUnit = 0, kGcn = 1, kEdge = 2 };
-// Epilogue of a row: none, mean (two roundings of the reference), or GIN's
-// self term out = fma(alpha, x[row], sum) — the reference's separate
-// tensor_add_inplace_ pass (agg_ops.cu:149-156) fused into the store.
-enum MeanMode : int { kNoMean = 0, kMeanDiv = 1, kMeanRcp = 2, kSelfAdd = 3 };
+enum MeanMode : int { kNoMean = 0, kMeanDiv = 1, kMeanRcp = 2 };
 
 struct SpmmArgs {
   const void* row_ptr;
@@ -139,8 +136,6 @@ struct SpmmArgs {
   int tiles;                // feature tiles (grid.y)
   int long_split;           // warps per segment (spmm.long_row_warps)
   int rows_per_warp;        // per-row kernel: rows a warp takes per block (2 or 4)
-  const float* self_x;      // kSelfAdd: the rows' own features (x + row_begin * f)
-  float self_alpha;         // kSelfAdd: 1 + eps
 };
 
 // Set by a segment whose bounded wait for its predecessor ran out (the row is
@@ -267,19 +262,6 @@ __device__ __forceinline__ float4 finish(float4 acc, int64_t deg) {
     }
   }
   return acc;
-}
-
-// The row epilogue with the row's identity: kSelfAdd reads float4 `cj` of row
-// r's own features and adds alpha times it with one fused multiply-add per
-// element, exactly as tensor_add_inplace_ would on the stored sum.
-template <int MEAN>
-__device__ __forceinline__ float4 finish_row(const SpmmArgs& a, float4 acc, int64_t deg, int64_t r, int64_t cj) {
-  if constexpr (MEAN == kSelfAdd) {
-    const float4 xv = ldg_f4(reinterpret_cast<const float4*>(a.self_x + r * a.f) + cj);
-    return fma4(a.self_alpha, xv, acc);
-  } else {
-    return finish<MEAN>(acc, deg);
-  }
 }
 
 // Lists the rows whose degree exceeds the long-row threshold: rows that fit
@@ -431,7 +413,7 @@ __device__ GNN_LONG_PHASE_INLINE void long_rows_phase(const SpmmArgs& a, float4*
         float4 s = s_part[j];
         for (int w = 1; w < split; ++w) s = add4(s, s_part[w * 32 * NV + j]);
         if (k > 0) s = add4(__ldcg(orow + cj), s);
-        if (last) s = finish_row<MEAN>(a, s, static_cast<int64_t>(end - beg), r, cj);
+        if (last) s = finish<MEAN>(s, static_cast<int64_t>(end - beg));
         orow[cj] = s;
       }
     }
@@ -530,7 +512,7 @@ __global__ void __launch_bounds__(kBlockThreads, resident_blocks<NV>())
     float4* orow = reinterpret_cast<float4*>(a.out + r * a.f);
 #pragma unroll
     for (int q = 0; q < NV; ++q) {
-      if (valid[q]) orow[col0 + 32 * q] = finish_row<MEAN>(a, acc[q], deg, r, col0 + 32 * q);
+      if (valid[q]) orow[col0 + 32 * q] = finish<MEAN>(acc[q], deg);
     }
   }
 }
@@ -618,7 +600,7 @@ __global__ void __launch_bounds__(kBlockThreads, resident_blocks<NV>()) spmm_str
         float4* orow = reinterpret_cast<float4*>(a.out + orow_id * a.f);
 #pragma unroll
         for (int q = 0; q < NV; ++q) {
-          if (valid[q]) orow[col0 + 32 * q] = finish_row<MEAN>(a, acc[q], d, orow_id, col0 + 32 * q);
+          if (valid[q]) orow[col0 + 32 * q] = finish<MEAN>(acc[q], d);
         }
       }
 #pragma unroll
@@ -784,7 +766,7 @@ __global__ void __launch_bounds__(384, 1) spmm_async_kernel(GNN_KPARAM SpmmArgs 
         float4* orow = reinterpret_cast<float4*>(a.out + orow_id * a.f);
 #pragma unroll
         for (int q = 0; q < NV; ++q) {
-          if (valid[q]) orow[col0 + 32 * q] = finish_row<MEAN>(a, acc[q], d, orow_id, col0 + 32 * q);
+          if (valid[q]) orow[col0 + 32 * q] = finish<MEAN>(acc[q], d);
         }
       }
 #pragma unroll
@@ -923,7 +905,6 @@ __global__ void __launch_bounds__(256) spmm_scalar_kernel(SpmmArgs a) {
       float v = acc[s];
       if (MEAN == kMeanDiv && deg > 0) v = __fdiv_rn(v, static_cast<float>(deg));
       if (MEAN == kMeanRcp && deg > 0) v = __fmul_rn(v, __fdiv_rn(1.0f, static_cast<float>(deg)));
-      if (MEAN == kSelfAdd) v = __fmaf_rn(a.self_alpha, a.self_x[r * a.f + fi], v);
       a.out[r * a.f + fi] = v;
     }
   }
@@ -1285,7 +1266,6 @@ struct SpmmRequest {
   int64_t row_begin;
   void* ws;
   size_t ws_bytes;
-  float self_alpha;  // kSelfAdd only
 };
 
 template <int WM, int MEAN, bool HOT, class IdxT>
@@ -1300,8 +1280,6 @@ int run_typed(const SpmmRequest& q, cudaStream_t stream) {
   a.hot = q.hot;
   a.hot_cutoff = q.hot_cutoff;
   a.sched = q.sched;
-  a.self_x = q.x + q.row_begin * q.f;
-  a.self_alpha = q.self_alpha;
   a.out = q.out;
   a.n = q.n;
   a.f = q.f;
@@ -1580,17 +1558,6 @@ extern "C" int gnn_spmm_sum_forward(const void* row_ptr, int row_ptr_type, const
   auto q = make_req(row_ptr, row_ptr_type, col_ind, nullptr, nullptr, x, out, num_nodes, num_edges,
                     feat_dim, workspace, workspace_bytes);
   return run<kUnit, kNoMean>(q, reinterpret_cast<cudaStream_t>(stream));
-}
-
-extern "C" int gnn_spmm_sum_self_forward(const void* row_ptr, int row_ptr_type, const int32_t* col_ind,
-                                         const float* x, float alpha, float* out, int64_t num_nodes,
-                                         int64_t num_edges, int64_t feat_dim, void* workspace,
-                                         size_t workspace_bytes, gnn_stream_t stream) {
-  GNN_REQUIRE(x == nullptr || x != out, GNN_ERR_INVALID_ARGUMENT, "out must not alias x");
-  auto q = make_req(row_ptr, row_ptr_type, col_ind, nullptr, nullptr, x, out, num_nodes, num_edges,
-                    feat_dim, workspace, workspace_bytes);
-  q.self_alpha = alpha;
-  return run<kUnit, kSelfAdd>(q, reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int gnn_spmm_mean_forward(const void* row_ptr, int row_ptr_type, const int32_t* col_ind,

@@ -216,17 +216,6 @@ int gnn_spmm_sum_forward(const void* row_ptr, int row_ptr_type, const int32_t* c
                          int64_t feat_dim, void* workspace, size_t workspace_bytes,
                          gnn_stream_t stream);
 
-/* GIN's aggregation in one pass: out[r] = fma(alpha, x[r], sum_e x[col_e]), i.e.
- * gnn_spmm_sum_forward followed by gnn_tensor_add_inplace(out, x, alpha) with
- * the same bits, without the second pass over [N, F]. No single reference
- * counterpart: it fuses the reference's spmm_sum_forward_ (agg_ops.cu:315) and
- * tensor_add_inplace_ (agg_ops.cu:399) as gin_inference.py calls them with
- * alpha = 1 + eps. out must not alias x. */
-int gnn_spmm_sum_self_forward(const void* row_ptr, int row_ptr_type, const int32_t* col_ind,
-                              const float* x, float alpha, float* out, int64_t num_nodes, int64_t num_edges,
-                              int64_t feat_dim, void* workspace, size_t workspace_bytes,
-                              gnn_stream_t stream);
-
 /* Mean aggregation (GraphSAGE); a row of degree 0 gives 0.
  * reciprocal == 0: acc / deg, as spmm_mean_forward_cuda_, agg_ops.cu:322 (kernel :40-45).
  * reciprocal != 0: acc * (1/deg), as spmm_mean_hmm_forward_cuda_, agg_ops.cu:336 (kernel :102-111). */

@@ -422,30 +422,3 @@ def test_dense_graph_two_rows_per_warp(f):
     finally:
         for k, v in zip(keys, old):
             N.config_set(k, v)
-
-
-@pytest.mark.parametrize("f,idx", [(128, torch.int32), (256, torch.int64), (31, torch.int32)])
-def test_sum_self_matches_sum_then_add(f, idx):
-    """spmm_sum_self_forward_ (GIN's aggregation and (1 + eps) x in one pass) gives
-    the bits of spmm_sum_forward_ followed by tensor_add_inplace_, on a graph with
-    long rows split into segments (F = 31 takes the scalar path)."""
-    n = 80_000
-    s, d = _hub_graph(n, [20_000, 9_000], extra=200_000, seed=51)
-    rp, ci, _ = O.plain_csr(s.numpy(), d.numpy(), n, add_self_loops=False)
-    x = synth.features(n, f, seed=52).to(DEV)
-    t_rp = torch.from_numpy(rp).to(DEV).to(idx)
-    t_ci = torch.from_numpy(ci).to(DEV)
-    old = N.config_get("spmm.long_row_threshold")
-    N.config_set("spmm.long_row_threshold", 300)
-    try:
-        for alpha in (1.0, 1.25):
-            ref = torch.empty(n, f, device=DEV)
-            agg_ops.spmm_sum_forward_(t_rp, t_ci, x, ref)
-            agg_ops.tensor_add_inplace_(ref, x, alpha)
-            got = torch.full((n, f), float("nan"), device=DEV)
-            agg_ops.spmm_sum_self_forward_(t_rp, t_ci, x, got, alpha)
-            assert torch.equal(got.view(torch.int32), ref.view(torch.int32)), alpha
-        with pytest.raises(RuntimeError, match="alias"):
-            agg_ops.spmm_sum_self_forward_(t_rp, t_ci, x, x, 1.0)
-    finally:
-        N.config_set("spmm.long_row_threshold", old)
