@@ -10,10 +10,12 @@
 //     the whole launch (staged once into shared memory, transposed to the
 //     K-major 128-byte-swizzled layout the MMA reads) and walks 128-row tiles of X;
 //   * warp 0 streams X tiles in 32-column (128-byte) swizzled chunks with TMA
-//     into a 4-stage ring; warp 1 issues tcgen05.mma (kind::tf32, M=128, N=BN,
+//     into a ring of up to 8 stages; warp 1 issues tcgen05.mma (kind::tf32, M=128, N=BN,
 //     K=8 per instruction) into one of two TMEM accumulators; warps 2-5 drain
-//     the other accumulator (tcgen05.ld), add bias, apply ReLU and store fp32
-//     rows — so loads, MMAs and the epilogue of consecutive tiles overlap;
+//     the other accumulator (tcgen05.ld), add bias, apply ReLU, write 32x32
+//     blocks into swizzled shared buffers (two per warp) and hand each block to
+//     a TMA bulk store, so the output leaves as whole 128-byte lines — loads,
+//     MMAs, the epilogue and the stores of consecutive tiles overlap;
 //   * every mbarrier wait is bounded by a clock deadline; on expiry the kernel
 //     records an error code in a device status word, stops issuing work, waits
 //     (bounded) for its in-flight copies and MMAs, frees its TMEM and returns.
@@ -38,6 +40,8 @@ constexpr int MAX_STAGES = 8;       // X chunk ring depth: runtime, up to this m
 constexpr size_t kSmemLimit = 227 * 1024;
 constexpr int A_STAGE_BYTES = BM * KCHUNK * 4;  // 16 KiB
 constexpr int kThreads = 192;       // warp0 TMA, warp1 MMA/TMEM, warps 2-5 epilogue
+constexpr int OUT_BLOCK_BYTES = 32 * 32 * 4;              // one 32-row x 32-column fp32 output block
+constexpr int OUT_STAGING_BYTES = 4 * 2 * OUT_BLOCK_BYTES;  // 4 epilogue warps x 2 buffers = 32 KiB
 constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 2 GHz
 
 // device status word: 0 ok, otherwise the role that gave up waiting
@@ -93,6 +97,19 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       ::"r"(smem_u32(dst)), "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
       : "memory");
 }
+
+// Bulk tensor store of one shared-memory block to global memory (rows past the
+// tensor's extent are clipped by the TMA unit), tracked in this thread's bulk group.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
+               ::"l"(map), "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// at most one committed store of this thread may still be reading shared memory
+__device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+// every committed store of this thread has completed
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -160,7 +177,8 @@ __device__ __forceinline__ void record_timeout(int code) { atomicCAS(&g_tc_statu
 
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_tf32_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const float* __restrict__ w, TcParams p) {
+    gemm_tf32_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_out,
+                        const float* __restrict__ w, TcParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int K = static_cast<int>(p.k);
@@ -169,7 +187,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sW = smem;                                  // K/32 blocks of [BN rows x 128 B], K-major
   const int S = p.stages;
   uint8_t* sA = smem + ((w_bytes + 1023) & ~1023u);    // S x 16 KiB
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sA + S * A_STAGE_BYTES);
+  uint8_t* sOut = sA + S * A_STAGE_BYTES;             // 4 warps x 2 x [32 rows x 128 B], swizzled
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + OUT_STAGING_BYTES);
   uint64_t* full = bars;                 // [S]
   uint64_t* empty = bars + S;            // [S]
   uint64_t* acc_full = bars + 2 * S;     // [2]
@@ -306,10 +325,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ---------------- epilogue: warps 2..5 ----------------
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int row_in_tile = 32 * q + lane;
+    // this warp's two staging buffers; lane L fills row L of a 32x32 block, its
+    // 16-byte chunk c at chunk c ^ (L % 8) (the TMA 128-byte swizzle), so the
+    // eight lanes of each shared-store phase hit eight different bank groups
+    uint8_t* staging = sOut + (warp - 2) * (2 * OUT_BLOCK_BYTES);
     int acc = 0;
     uint32_t acc_phase = 0;
-    const int64_t ncol0 = static_cast<int64_t>(n_tile) * BN;
+    uint32_t blocks = 0;  // stores this warp has committed
+    const int ncol0 = n_tile * BN;
     for (int64_t mt = m_first; mt < p.m_tiles; mt += m_step) {
       // warp-uniform decision: the tcgen05.ld below is .sync.aligned
       if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[acc], acc_phase))) {
@@ -317,13 +340,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      const int64_t row = mt * BM + row_in_tile;
-      float* orow = p.out + row * p.n + ncol0;
+      const int64_t row0 = mt * BM + 32 * q;  // first row of this warp's lane quarter
+      const bool has_rows = row0 < p.m;        // rows past m are clipped by the store
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
         uint32_t r[32];
         tmem_ld32(tmem_base + static_cast<uint32_t>(acc * BN + c0) + (static_cast<uint32_t>(32 * q) << 16), r);
-        if (row < p.m) {
+        if (has_rows) {
+          uint8_t* buf = staging + (blocks & 1) * OUT_BLOCK_BYTES;
+          // the store committed two blocks ago read this buffer: it must be done reading
+          if (lane == 0) bulk_wait_read_1();
+          __syncwarp();
 #pragma unroll
           for (int j = 0; j < 32; j += 4) {
             float4 v = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
@@ -335,8 +362,16 @@ __global__ void __launch_bounds__(kThreads, 1)
               v.z = v.z < 0.0f ? 0.0f : v.z;
               v.w = v.w < 0.0f ? 0.0f : v.w;
             }
-            *reinterpret_cast<float4*>(orow + c0 + j) = v;
+            *reinterpret_cast<float4*>(buf + lane * 128 + ((((j >> 2) ^ (lane & 7))) << 4)) = v;
           }
+          // generic-proxy shared writes -> visible to the TMA unit (async proxy)
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmap_out, buf, ncol0 + c0, static_cast<int>(row0));
+            bulk_commit();
+          }
+          ++blocks;
         }
       }
       tc_fence_before();
@@ -345,6 +380,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
+    // shared staging must outlive the stores reading it; the writes land before exit
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
   }
 
   __syncthreads();
@@ -403,7 +441,7 @@ bool shape_ok(int64_t m, int64_t k, int64_t n) {
 
 size_t smem_bytes_for(int bn, int64_t k, int stages) {
   const size_t w = ((static_cast<size_t>(bn) * k * 4) + 1023) & ~size_t(1023);
-  return 1024 /* alignment slack */ + w + static_cast<size_t>(stages) * A_STAGE_BYTES +
+  return 1024 /* alignment slack */ + w + static_cast<size_t>(stages) * A_STAGE_BYTES + OUT_STAGING_BYTES +
          256 /* barriers + TMEM slot */;
 }
 
@@ -439,6 +477,18 @@ int launch_bn(const float* x, const float* w, const float* bias, float* out, int
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(GNN_ERR_CUDA, "cuTensorMapEncodeTiled(x) failed: " + std::to_string(r));
   }
+  // output [m, n] row-major, written in 32-row x 32-column blocks (x = column, a multiple of 32)
+  CUtensorMap to{};
+  {
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(n), static_cast<cuuint64_t>(m)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(n) * 4};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(&to, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, out, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(GNN_ERR_CUDA, "cuTensorMapEncodeTiled(out) failed: " + std::to_string(r));
+  }
   const size_t smem = smem_bytes(BN, k);
   // the opt-in is a per-device function attribute; remember the largest size set per device
   static int configured_smem[64][3] = {};
@@ -469,7 +519,7 @@ int launch_bn(const float* x, const float* w, const float* bias, float* out, int
   const int64_t tiles = p.m_tiles * p.n_tiles;
   int64_t ctas = std::min<int64_t>(tiles, sm_count());
   ctas = std::max<int64_t>(p.n_tiles, (ctas / p.n_tiles) * p.n_tiles);
-  gemm_tf32_tc_kernel<BN><<<static_cast<unsigned>(ctas), kThreads, smem, stream>>>(tx, w, p);
+  gemm_tf32_tc_kernel<BN><<<static_cast<unsigned>(ctas), kThreads, smem, stream>>>(tx, to, w, p);
   GNN_LAUNCH_CHECK("gemm_tf32_tc_kernel launch");
   return GNN_OK;
 }
