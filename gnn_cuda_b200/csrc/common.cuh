@@ -70,11 +70,37 @@ int sm_count();
 // ---- device helpers ---------------------------------------------------------------
 __device__ __forceinline__ float4 ldg_f4(const float4* p) { return __ldg(p); }
 
-// Streaming (read-once) loads for index/weight arrays: do not keep them in L1.
+// Streaming (read-once) loads for index/weight arrays: do not keep them in L1
+// (and, with GNN_STREAM_EVICT_FIRST, mark their L2 lines first to go).
+#ifndef GNN_STREAM_EVICT_FIRST
+#define GNN_STREAM_EVICT_FIRST 0
+#endif
 __device__ __forceinline__ int ld_stream_i32(const int32_t* p) {
   int v;
+#if GNN_STREAM_EVICT_FIRST
+  asm volatile(
+      "{\n\t.reg .b64 pol;\n\t"
+      "createpolicy.fractional.L2::evict_first.b64 pol, 1.0;\n\t"
+      "ld.global.nc.L1::no_allocate.L2::cache_hint.b32 %0, [%1], pol;\n\t}"
+      : "=r"(v)
+      : "l"(p));
+#else
   asm volatile("ld.global.nc.L1::no_allocate.b32 %0, [%1];" : "=r"(v) : "l"(p));
+#endif
   return v;
+}
+
+// Aggregation output rows are written once per launch; with GNN_SPMM_STORE_CS
+// they are stored with the streaming (evict-first) cache operator.
+#ifndef GNN_SPMM_STORE_CS
+#define GNN_SPMM_STORE_CS 0
+#endif
+__device__ __forceinline__ void st_out_f4(float4* p, float4 v) {
+#if GNN_SPMM_STORE_CS
+  __stcs(p, v);
+#else
+  *p = v;
+#endif
 }
 __device__ __forceinline__ float ld_stream_f32(const float* p) {
   float v;

@@ -414,7 +414,7 @@ __device__ GNN_LONG_PHASE_INLINE void long_rows_phase(const SpmmArgs& a, float4*
         for (int w = 1; w < split; ++w) s = add4(s, s_part[w * 32 * NV + j]);
         if (k > 0) s = add4(__ldcg(orow + cj), s);
         if (last) s = finish<MEAN>(s, static_cast<int64_t>(end - beg));
-        orow[cj] = s;
+        st_out_f4(orow + cj, s);
       }
     }
     if (!last) {
@@ -512,7 +512,7 @@ __global__ void __launch_bounds__(kBlockThreads, resident_blocks<NV>())
     float4* orow = reinterpret_cast<float4*>(a.out + r * a.f);
 #pragma unroll
     for (int q = 0; q < NV; ++q) {
-      if (valid[q]) orow[col0 + 32 * q] = finish<MEAN>(acc[q], deg);
+      if (valid[q]) st_out_f4(orow + col0 + 32 * q, finish<MEAN>(acc[q], deg));
     }
   }
 }
@@ -600,7 +600,7 @@ __global__ void __launch_bounds__(kBlockThreads, resident_blocks<NV>()) spmm_str
         float4* orow = reinterpret_cast<float4*>(a.out + orow_id * a.f);
 #pragma unroll
         for (int q = 0; q < NV; ++q) {
-          if (valid[q]) orow[col0 + 32 * q] = finish<MEAN>(acc[q], d);
+          if (valid[q]) st_out_f4(orow + col0 + 32 * q, finish<MEAN>(acc[q], d));
         }
       }
 #pragma unroll
@@ -766,7 +766,7 @@ __global__ void __launch_bounds__(384, 1) spmm_async_kernel(GNN_KPARAM SpmmArgs 
         float4* orow = reinterpret_cast<float4*>(a.out + orow_id * a.f);
 #pragma unroll
         for (int q = 0; q < NV; ++q) {
-          if (valid[q]) orow[col0 + 32 * q] = finish<MEAN>(acc[q], d);
+          if (valid[q]) st_out_f4(orow + col0 + 32 * q, finish<MEAN>(acc[q], d));
         }
       }
 #pragma unroll
