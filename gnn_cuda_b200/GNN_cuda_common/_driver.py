@@ -17,6 +17,7 @@ from torch import nn
 
 from .allocator import COMPUTE_MEMORY_MODES, GRAPH_MEMORY_MODES, normalize_memory_mode, pointer_info
 
+# the reference drivers' --data_root default (gcn_inference.py:197), kept so scripts that rely on it still work
 DEFAULT_DATA_ROOT = "/root/workspace/mnt/dataset_npz"
 
 
