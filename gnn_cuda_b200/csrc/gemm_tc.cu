@@ -20,7 +20,7 @@
 //     records an error code in a device status word, stops issuing work, waits
 //     (bounded) for its in-flight copies and MMAs, frees its TMEM and returns.
 // Accuracy: inputs are consumed as TF32 (10-bit mantissa), products accumulate
-// in fp32 — within the 2e-3 relative bound of the north-star tolerance.
+// in fp32 — within a relative error of 2e-3 of the float64 product (scaled by sum_k |x_ik * w_kj|).
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>

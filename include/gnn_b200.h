@@ -58,7 +58,7 @@ typedef enum gnn_index_type {
 
 /* Precision of the dense transform X·W on the tensor cores. */
 typedef enum gnn_precision {
-  GNN_PRECISION_TF32 = 0, /* one tf32 tcgen05 pass (north-star tolerance 2e-3)   */
+  GNN_PRECISION_TF32 = 0, /* one tf32 tcgen05 pass (relative tolerance 2e-3)     */
   GNN_PRECISION_FP32 = 1  /* fp32 SIMT FFMA, the reference's cublasSgemm numerics */
 } gnn_precision;
 

@@ -11,7 +11,7 @@ the sources are compiled exactly where they lie under the reference checkout,
 with ``-O3 -std=c++17`` and the architecture list the reference would pick on a
 B200 (compute capability 10.0, ``loader.py:42-44``). Nothing is copied into
 this repository; the build products go only to ``oracle/_ref/`` (git-ignored,
-but shipped to the GPU box with the rest of the tree).
+but shipped to the GPU machine with the rest of the tree).
 
 Usage:  python oracle/build_ref.py [--reference /root/reference] [--jobs 3]
 """

@@ -1,7 +1,7 @@
 """CPU oracle for the UVM locality preprocessing (row schedule, page metadata,
 co-access order, hot-prefix partition).
 
-TEST INFRASTRUCTURE ONLY — the checker, never the product. Only ``tests/``
+TEST INFRASTRUCTURE ONLY — the test oracle, never the product. Only ``tests/``
 import this module; nothing under ``gnn_cuda_b200/`` may import it.
 
 A vectorised numpy restatement of the reference's host implementation,

@@ -2,7 +2,7 @@
 """Generate the CSR golden vectors by running the reference's own builders.
 
 Imports ``GNN_cuda_common/graph_utils.py`` from the reference checkout (read
-only, in the development container; the GPU box never runs this) and records,
+only, in the development container; GPU test runs never run this) and records,
 for a set of small edge lists that cover the edge cases of the CSR contract
 (duplicate edges, pre-existing self-loops, isolated nodes, a single node, an
 empty edge list, a power-law graph), the outputs of

@@ -3,7 +3,7 @@
 reference's own host implementation.
 
 Imports ``GNN_cuda_common/graph_utils.py`` from the reference checkout (read
-only, in the development container; the GPU box never runs this) and records,
+only, in the development container; GPU test runs never run this) and records,
 for small edge lists and several parameter sets, the outputs of
   build_page_reuse_schedule_metadata      (graph_utils.py:244-372)
   build_coaccess_feature_permutation      (graph_utils.py:375-446)

@@ -2,7 +2,7 @@
 
 FP32 precision: the FFMA kernel accumulates k in increasing order, exactly
 like the oracle's fmaf loop, so results are compared bit for bit. TF32
-precision (tensor cores) is held to the north-star 2e-3 relative tolerance,
+precision (tensor cores) is held to a 2e-3 relative tolerance,
 measured against the float64 product and scaled by sum_k |x_ik * w_kj|.
 Elementwise ops are bit-exact with the reference arithmetic.
 """

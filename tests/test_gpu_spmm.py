@@ -4,7 +4,7 @@ Bit-exact checks: rows accumulated by one warp follow the reference's CSR
 order, so they must equal the oracle's fmaf/add sequence bit for bit; long
 rows follow the documented warp split, which the oracle reproduces with
 ``split_warps`` — so every output element is compared exactly. Every case is
-also held to the north-star fp32 tolerance against float64.
+also held to the fp32 tolerance of 1e-5 (relative to the summed magnitudes) against float64.
 """
 import ctypes
 

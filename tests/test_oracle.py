@@ -2,7 +2,7 @@
 
 * sum / mean are checked against a pure-Python float32 loop in CSR order on a
   small graph (exact: float32 additions in the same order give the same bits);
-* every mode is checked against the float64 aggregation within the north-star
+* every mode is checked against the float64 aggregation within the
   fp32 tolerance |ours - f64| <= 1e-5 * (sum|terms| + |f64|);
 * the long-row split schedule equals plain CSR order on rows below the
   threshold, and stays within the same tolerance above it.
