@@ -79,6 +79,31 @@ def test_config_knobs():
         N.config_set("spmm.long_row_warps", 64)
 
 
+@pytest.mark.parametrize("name,default,good,bad", [
+    ("spmm.long_row_threshold", 0, [0, 1, 8192], [-1]),
+    ("spmm.long_row_warps", 16, [4, 8, 16], [3, 17]),
+    ("spmm.kernel", 1, [0, 1, 2], [-1, 3]),
+    ("spmm.schedule", 3, [0, 1, 2, 3], [-1, 4]),
+    ("spmm.schedule_window", 2048, [1024, 4096, 2**30], [1023, 2**30 + 1]),
+    ("gemm.stages", 0, [0, 2, 5, 8], [1, 9, -1]),
+])
+def test_config_knob_ranges(name, default, good, bad):
+    """Every tuning knob: its default, accepted values, and a refusal that leaves the value unchanged."""
+    old = N.config_get(name)
+    assert old == default
+    try:
+        for v in good:
+            N.config_set(name, v)
+            assert N.config_get(name) == v
+        N.config_set(name, default)
+        for v in bad:
+            with pytest.raises(RuntimeError, match=name.replace(".", r"\.")):
+                N.config_set(name, v)
+            assert N.config_get(name) == default
+    finally:
+        N.config_set(name, old)
+
+
 def test_python_checks_match_reference_messages():
     from gnn_cuda_b200.GNN_cuda_common import agg_ops, gcn_ops
     rp = torch.zeros(3, dtype=torch.int32)
