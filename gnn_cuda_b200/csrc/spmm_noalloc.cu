@@ -6,10 +6,17 @@
 // input/output buffers in; a process running at a fixed device-memory budget;
 // or a latency-sensitive path that must not call cudaMalloc/cudaFree, which can
 // block until the whole device is idle. gnn_spmm_gcn_forward_noalloc serves
-// them: it runs the same kernels with the same results, and takes its scratch
-// from the fixed-size array below, which the CUDA runtime places in device
-// memory when this module is loaded on a device and which stays there until
-// the process exits. Nothing is allocated per call.
+// them: it runs exactly what gnn_spmm_gcn_forward runs when given the minimum
+// workspace (gnn_spmm_workspace_bytes), with the same results, and takes that
+// workspace from the fixed-size array below, which the CUDA runtime places in
+// device memory when this module is loaded on a device and which stays there
+// until the process exits. Nothing is allocated per call.
+//
+// Because only the minimum workspace is used, the per-row kernel takes rows in
+// row-id order: the degree-ordered row schedule needs another 4 bytes per node
+// (18,102,528 bytes in all for a 2,449,029-node, 64,308,169-entry graph, more
+// than the array holds), so it never runs here. On power-law graphs that costs
+// time, not accuracy (every row is summed the same way in either order).
 //
 // Limits and sharing rules (also in include/gnn_b200.h):
 //   * the array holds kNoAllocScratchBytes (8 MiB); problems whose
@@ -24,7 +31,9 @@
 //     do not matter; the rest of the array is written before it is read;
 //   * the first call on each device looks the array's device address up
 //     (cudaGetSymbolAddress); make that first call before any stream capture
-//     on that device.
+//     on that device. The address is kept for the life of the process, so a
+//     cudaDeviceReset of that device after the first call is not supported
+//     (the module is reloaded and the array may move).
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -86,6 +95,7 @@ extern "C" int gnn_spmm_gcn_forward_noalloc(const void* row_ptr, int row_ptr_typ
   void* scratch = nullptr;
   const int rc = scratch_for_current_device(&scratch);
   if (rc != GNN_OK) return rc;
+  // exactly the minimum workspace: the same launches as gnn_spmm_gcn_forward given need bytes
   return gnn_spmm_gcn_forward(row_ptr, row_ptr_type, col_ind, deg_inv_sqrt, x, out, num_nodes, num_edges,
-                              feat_dim, scratch, kNoAllocScratchBytes, stream);
+                              feat_dim, scratch, need, stream);
 }

@@ -142,15 +142,22 @@ int gnn_spmm_gcn_partition_forward(const void* row_ptr, int row_ptr_type, const 
  * binding that owns all device memory and passes only inputs and outputs, a
  * process pinned to a fixed memory budget, or a latency-critical path that
  * cannot afford cudaMalloc/cudaFree (which may wait for the whole device).
- * Same kernels and results as gnn_spmm_gcn_forward; the scratch is a built-in
- * 8 MiB (8388608-byte) device array per GPU, held until the process exits.
+ * Same kernels and results as gnn_spmm_gcn_forward given the minimum workspace
+ * (gnn_spmm_workspace_bytes): rows run in row-id order, because the
+ * degree-ordered row schedule needs 4 more bytes per node than the scratch
+ * holds at large sizes (18,102,528 bytes for the 2,449,029-node graph below),
+ * which is slower on power-law graphs but gives the same results. The scratch
+ * is a built-in 8 MiB (8388608-byte) device array per GPU, held until the
+ * process exits.
  * Problems with gnn_spmm_workspace_bytes(num_nodes, num_edges) > 8 MiB are
  * rejected with GNN_ERR_UNSUPPORTED (for example, any graph with at most
  * 1,000,000 nodes and 500,000,000 entries fits, and so does a 2,449,029-node,
  * 64,308,169-entry graph). All calls on a device share that array: calls that
  * overlap on the GPU race and must be serialised (e.g. one stream). Each call
  * clears the counters it reads. The first call on a device looks the array's
- * address up, so make it before any stream capture on that device. */
+ * address up, so make it before any stream capture on that device; that
+ * address is kept for the process's life, so a cudaDeviceReset of the device
+ * after the first call is not supported. */
 int gnn_spmm_gcn_forward_noalloc(const void* row_ptr, int row_ptr_type, const int32_t* col_ind,
                                  const float* deg_inv_sqrt, const float* x, float* out,
                                  int64_t num_nodes, int64_t num_edges, int64_t feat_dim,

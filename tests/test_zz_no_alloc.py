@@ -25,19 +25,26 @@ pytestmark = pytest.mark.gpu
 DEV = torch.device("cuda", 0)
 
 
-@pytest.fixture
-def hub_graph():
-    n, f = 6000, 128
+def _hub_graph(n: int, f: int = 128):
     g = torch.Generator().manual_seed(77)
     # node 0 is a hub of degree n-1; the rest is a sparse random graph
-    u = torch.cat([torch.zeros(n - 1, dtype=torch.int64), torch.randint(1, n, (20000,), generator=g)])
-    v = torch.cat([torch.arange(1, n, dtype=torch.int64), torch.randint(1, n, (20000,), generator=g)])
+    m = max(20000, 4 * n)
+    u = torch.cat([torch.zeros(n - 1, dtype=torch.int64), torch.randint(1, n, (m,), generator=g)])
+    v = torch.cat([torch.arange(1, n, dtype=torch.int64), torch.randint(1, n, (m,), generator=g)])
     keep = u != v
     key = torch.unique(torch.minimum(u[keep], v[keep]) * n + torch.maximum(u[keep], v[keep]))
     s, d = synth.symmetrize(key // n, key % n)
     rp, ci, dis = synth.csr_on_device(s, d, n, add_self_loops=True)
     x = synth.features(n, f, seed=78)
     return {k: t.to(DEV).contiguous() for k, t in dict(rp=rp, ci=ci, dis=dis, x=x).items()} | {"n": n, "f": f}
+
+
+# 6,000 nodes: below the size at which the workspace entry point builds a
+# degree-ordered row schedule; 70,000 nodes: above it, where only a workspace
+# larger than the minimum would enable that schedule
+@pytest.fixture(params=[6000, 70000])
+def hub_graph(request):
+    return _hub_graph(request.param)
 
 
 def _ptr(t):
@@ -52,6 +59,7 @@ def test_noalloc_matches_workspace_entry_point_twice(hub_graph):
     N.config_set("spmm.long_row_threshold", 64)  # the hub and many rows go through the scratch list
     try:
         stream = torch.cuda.current_stream(DEV).cuda_stream
+        # the minimum workspace, which is what the allocation-free entry point uses
         ws_bytes = L.gnn_spmm_workspace_bytes(n, nnz)
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=DEV)
         ref = torch.empty(n, f, device=DEV)
