@@ -66,6 +66,10 @@ def parse_args():
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU-baseline sample time (0: skip)")
     ap.add_argument("--scale", type=float, default=1.0, help="scale the graph down (smoke runs only)")
+    ap.add_argument("--no-check", dest="check", action="store_false",
+                    help="skip the check of sampled output rows against the oracle after the timed region")
+    ap.add_argument("--no-reference-gpu", dest="reference_gpu", action="store_false",
+                    help="skip timing the reference's own CUDA kernels on the same tensors")
     ap.add_argument("--chunks", type=int, default=0,
                     help="row pieces per rank, exchanged as they finish (N > 1; 0: 2 from 8 GPUs up, else 1)")
     ap.add_argument("--exchange", choices=["push", "halo", "allgather"], default="halo",
@@ -181,8 +185,9 @@ def build_problem(seed: int, device: torch.device, scale: float):
     x = synth.features(n, FEAT, seed=seed + 1, device=device)
     ws = [synth.glorot(FEAT, FEAT, seed=seed + 10 + li, device=device) for li in range(LAYERS)]
     bs = [torch.zeros(FEAT, device=device) for _ in range(LAYERS)]
-    torch.cuda.synchronize(device)
-    log(f"[bench] graph n={n} nnz={ci.numel()} built in {time.time() - t0:.1f}s")
+    if device.type == "cuda":
+        torch.cuda.synchronize(device)
+    log(f"[bench] graph n={n} nnz={ci.numel()} built on {device.type} in {time.time() - t0:.1f}s")
     return dict(n=n, nnz=int(ci.numel()), rp=rp, ci=ci, dis=dis, x=x, ws=ws, bs=bs)
 
 
@@ -196,9 +201,11 @@ def row_order() -> str:
 
 
 def describe(prob, world: int, gemm: str | None = None, chunks: int = 1, exchange: str = "halo",
-             transport: str = "sm", layout: str = "balanced") -> dict:
+             transport: str = "sm", layout: str = "balanced", order: str | None = None) -> dict:
     if gemm is None:
         gemm = "tcgen05-tf32" if N.lib().gnn_gemm_uses_tensor_cores(prob["n"], FEAT, FEAT) else "ffma-fp32"
+    if order is None:
+        order = row_order()
     return {"workload": f"{WORKLOAD}: GCN {LAYERS} layers {FEAT}->{FEAT}->{FEAT}, ReLU between layers",
             "nodes": prob["n"], "csr_entries": int(prob["nnz"]), "feat_dim": FEAT, "layers": LAYERS,
             "self_loops": True, "graph": "R-MAT(0.57,0.19,0.19,0.05), symmetrised, de-duplicated",
@@ -207,7 +214,7 @@ def describe(prob, world: int, gemm: str | None = None, chunks: int = 1, exchang
                                              f"+{layout}_halo_push_pieces{chunks}" if exchange == "halo" else
                                              f"+{layout}_nccl_allgather_pieces{chunks}"),
             "l2": "inputs larger than L2 (X is %.2f GB), no flush" % (prob["n"] * FEAT * 4 / 1e9),
-            "gemm": gemm, "row_order": row_order()}
+            "gemm": gemm, "row_order": order}
 
 
 # ---------------------------------------------------------------------------
@@ -294,6 +301,10 @@ def run_ours(args, rank: int, world: int, device: torch.device):
         dist.barrier()
     launches = N.lib().gnn_kernel_launches() - launches0
     ms_total = t_start.elapsed_time(t_end)
+    parity = None
+    if world == 1 and args.check:
+        # the last timed step left h1 in out0, the layer-2 aggregate in agg, the output in out1
+        parity = check_forward_sample(prob, bufs["out0"], bufs["agg"], bufs["out1"], device)
     # SpMM time per layer on this rank (summed over its row pieces when N > 1)
     spmm_ms = [b.elapsed_time(e) for b, e in timers.get("spmm", [])]
     spmm_ms_avg = sum(spmm_ms) / max(1, args.steps * LAYERS)
@@ -417,9 +428,173 @@ def run_ours(args, rank: int, world: int, device: torch.device):
         "gpu_launches": int(launches),
         "clocks": clocks.summary(),
     }
+    if parity is not None:
+        result["parity"] = parity
+    if world == 1 and args.reference_gpu:
+        result["reference_gpu"] = reference_gpu_baseline(prob, device, args.seed, args.scale)
     if world == 1 and args.cpu_seconds > 0:
         result["cpu_baseline"] = cpu_baseline(prob, args.cpu_seconds)
     return result
+
+
+# ---------------------------------------------------------------------------
+# output check of the timed forward (after the timed region; the oracle is the checker)
+# ---------------------------------------------------------------------------
+
+def auto_long_threshold(nnz: int, device) -> int:
+    """The engine's automatic long-row threshold, clamp(nnz / (SMs * 32 * 8), 256, 8192)."""
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    return max(32, min(8192, max(256, nnz // (sms * 32 * 8))))
+
+
+def check_forward_sample(prob, h1: torch.Tensor, agg2: torch.Tensor, out: torch.Tensor, device,
+                         n_short: int = 4000, seed: int = 7) -> dict:
+    """Sampled rows of the forward just timed, against the oracle.
+
+    Every row above the long-row threshold plus `n_short` others. The layer-2
+    aggregation (agg2 = aggregate(h1), the GPU's own layer-1 output) is compared
+    bit for bit with the oracle's restatement of this engine's schedule and held
+    to 1e-5 of float64; the layer-1 output h1 and the final output are held to
+    the TF32 tolerance (2e-3 of sum |a w|) against float64 transforms of the
+    oracle's aggregates of the same rows."""
+    from oracle import oracle as O
+    rp, ci, dis, x = prob["rp"], prob["ci"], prob["dis"], prob["x"]
+    thr = auto_long_threshold(int(ci.numel()), device)
+    deg = (rp[1:] - rp[:-1]).to(torch.int64)
+    long_rows = torch.nonzero(deg > thr).flatten()
+    short = torch.nonzero(deg <= thr).flatten()
+    g = torch.Generator(device=device).manual_seed(seed)
+    short = short[torch.randperm(short.numel(), generator=g, device=device)[:n_short]]
+    rows = torch.cat([long_rows, short]).cpu().numpy()
+    k = rows.size
+    idx = torch.as_tensor(rows, device=device)
+    w = [t.cpu().numpy().astype(np.float64) for t in prob["ws"]]
+    b = [t.cpu().numpy().astype(np.float64) for t in prob["bs"]]
+
+    def tf32_err(got, a32, li, relu):
+        a = a32.astype(np.float64)
+        exp = a @ w[li] + b[li]
+        if relu:
+            exp = np.maximum(exp, 0.0)
+        scale = np.abs(a) @ np.abs(w[li]) + np.abs(b[li]) + 1e-30
+        return float(np.max(np.abs(got.astype(np.float64) - exp) / scale))
+
+    # layer 1: the oracle's aggregate of x on these rows, then the transform
+    srp, sci, sx, sdis = O.compact_rows_problem(rp, ci, x, rows, dis)
+    agg1 = O.spmm(srp, sci, sx, mode=O.W_GCN, dis=sdis, split_warps=16, long_thr=thr, rows=(0, k))
+    err_h1 = tf32_err(h1[idx].cpu().numpy(), agg1, 0, True)
+    # layer 2: aggregate of the GPU's h1, bit for bit
+    srp, sci, sh, sdis = O.compact_rows_problem(rp, ci, h1, rows, dis)
+    exp2 = O.spmm(srp, sci, sh, mode=O.W_GCN, dis=sdis, split_warps=16, long_thr=thr, rows=(0, k))
+    got2 = agg2[idx].cpu().numpy()
+    same = np.all(got2.view(np.uint32) == exp2.view(np.uint32), axis=1)
+    f64, ab = O.spmm_f64_rows(srp, sci, sh, np.arange(k), mode=O.W_GCN, dis=sdis)
+    err_agg = O.check_close_to_f64(got2, f64, ab, rel=1e-5)
+    err_out = tf32_err(out[idx].cpu().numpy(), got2, 1, False)
+    nl = int(long_rows.numel())
+    return {"rows_checked": int(k), "long_rows_checked": nl, "long_row_threshold": thr,
+            "agg_bit_exact_rows": int(same.sum()), "bit_exact_short_rows": bool(same[nl:].all()),
+            "bit_exact_long_rows": bool(same[:nl].all()),
+            "agg_err_vs_f64": round(err_agg, 4), "agg_tolerance": "|ours - f64| <= 1e-5 (sum|w x| + |f64|); "
+            "the figure is the worst ratio to that bound (<= 1 passes)",
+            "max_rel_err": round(max(err_h1, err_out), 6), "tf32_tolerance": 2e-3,
+            "ok": bool(same.all() and err_agg <= 1.0 and max(err_h1, err_out) <= 2e-3),
+            "checked": "layer-1 output (TF32) and layer-2 aggregation (bits) and output (TF32) of the last timed "
+                       "step, sampled rows (every long row + random others), against the C oracle"}
+
+
+# ---------------------------------------------------------------------------
+# the reference's own GPU kernels, timed on the same box and tensors
+# ---------------------------------------------------------------------------
+
+REF_SO = ROOT / "oracle" / "_ref"
+
+
+def _load_ref(name: str):
+    import importlib.machinery
+    import importlib.util
+    path = REF_SO / f"{name}.so"
+    if not path.exists():
+        return None
+    loader = importlib.machinery.ExtensionFileLoader(name, str(path))
+    spec = importlib.util.spec_from_loader(name, loader)
+    mod = importlib.util.module_from_spec(spec)
+    loader.exec_module(mod)
+    return mod
+
+
+def _median_ms(fn, device, reps: int = 10, warm: int = 3) -> float:
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize(device)
+    times = []
+    for _ in range(reps):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1))
+    return float(statistics.median(times))
+
+
+def reference_gpu_baseline(prob, device, seed: int, scale: float = 1.0) -> dict:
+    """The reference's own CUDA kernels (compiled from its sources, unmodified) and
+    this library's kernel for the same call, each timed alone with CUDA events on
+    the same device tensors: median of 10 calls after 3 warm-up calls."""
+    ref = {n: _load_ref(n) for n in ("ref_gcn_ops", "ref_pyg_gcn_ops", "ref_agg_ops")}
+    if any(m is None for m in ref.values()):
+        return {"unavailable": "the reference kernels are not built into oracle/_ref (python oracle/build_ref.py)"}
+    from gnn_cuda_b200.GNN_cuda_common import pyg_gcn_ops
+    rp, ci, dis, x = prob["rp"], prob["ci"], prob["dis"], prob["x"]
+    n = prob["n"]
+    out = torch.empty(n, FEAT, device=device)
+    res: dict = {}
+
+    def pair(name, theirs, ours, what):
+        t_ref = _median_ms(theirs, device)
+        t_ours = _median_ms(ours, device)
+        res[name] = {"call": what, "reference_ms": round(t_ref, 4), "ours_ms": round(t_ours, 4),
+                     "speedup": round(t_ref / t_ours, 3)}
+
+    pair("gcn_aggregation", lambda: ref["ref_gcn_ops"].spmm_gcn_hmm_forward_(rp, ci, dis, x, out),
+         lambda: gcn_ops.spmm_gcn_forward_(rp, ci, dis, x, out),
+         "spmm_gcn_hmm_forward_ (gcn_spmm_hmm_kernel, gcn_ops.cu:34-109), products-shaped graph, F = 128")
+    rows_of = torch.repeat_interleave(torch.arange(n, device=device), (rp[1:] - rp[:-1]).to(torch.int64))
+    ew = dis[rows_of] * dis[ci.to(torch.int64)]
+    del rows_of
+    pair("pyg_gcn_aggregation", lambda: ref["ref_pyg_gcn_ops"].spmm_pyg_gcn_plain_forward_(rp, ci, ew, x, out),
+         lambda: pyg_gcn_ops.spmm_pyg_gcn_forward_(rp, ci, ew, x, out, spmm_mode="plain"),
+         "spmm_pyg_gcn_plain_forward_ (pyg_gcn_ops.cu:33-108), products-shaped graph, F = 128")
+    del ew
+    pair("sum_aggregation", lambda: ref["ref_agg_ops"].spmm_sum_forward_(rp, ci, x, out),
+         lambda: agg_ops.spmm_sum_forward_(rp, ci, x, out),
+         "spmm_sum_forward_ (csr_agg_kernel<false>, agg_ops.cu:23-47), products-shaped graph, F = 128")
+    agg = torch.empty(n, FEAT, device=device)
+    gcn_ops.spmm_gcn_forward_(rp, ci, dis, x, agg)
+    w = prob["ws"][0]
+    pair("gemm", lambda: ref["ref_agg_ops"].gemm_forward_(agg, w, out), lambda: agg_ops.gemm_forward_(agg, w, out),
+         f"gemm_forward_ (cublasSgemm FP32 with a handle created per call, agg_ops.cu:369-391) vs this library's "
+         f"tcgen05 TF32 GEMM, {n} x {FEAT} x {FEAT}")
+    del agg, out
+    torch.cuda.empty_cache()
+    # the Reddit-shaped mean aggregation (the GraphSAGE configuration), F = 256
+    src, dst, nr = synth.make_graph("sage_reddit_like", seed=seed, device=device, scale_nodes=scale)
+    rrp, rci, _ = synth.csr_on_device(src, dst, nr, add_self_loops=False)
+    del src, dst
+    rx = synth.features(nr, SAGE_FEAT, seed=seed + 1, device=device)
+    rout = torch.empty(nr, SAGE_FEAT, device=device)
+    torch.cuda.empty_cache()
+    pair("mean_aggregation", lambda: ref["ref_agg_ops"].spmm_mean_forward_(rrp, rci, rx, rout),
+         lambda: agg_ops.spmm_mean_forward_(rrp, rci, rx, rout),
+         f"spmm_mean_forward_ (csr_agg_kernel<true>, agg_ops.cu:23-47), Reddit-shaped graph ({nr} nodes, "
+         f"{rci.numel()} entries), F = {SAGE_FEAT}")
+    del rrp, rci, rx, rout
+    torch.cuda.empty_cache()
+    res["note"] = ("each kernel timed alone on the same seeded device tensors (inputs larger than L2); reference "
+                   "kernels compiled unmodified from the reference's sources by oracle/build_ref.py")
+    return res
 
 
 # ---------------------------------------------------------------------------
@@ -473,13 +648,16 @@ def cpu_baseline(prob, seconds: float) -> dict:
                       f"({_sample_bytes(hp, rows) / 1e9:.2f} algorithmic GB) in {dt:.2f} s; C oracle, OpenMP"}
 
 
-def run_reference(args, device: torch.device):
+def run_reference(args):
+    """The reference arm: its CPU arithmetic (the C restatement) on the host's
+    cores. Inputs are built on the host with torch CPU ops (same generator and
+    shape as the GPU arm, the host's random stream); no GPU and nothing of this
+    library is used."""
     from oracle import oracle as O
-    prob = build_problem(args.seed, device, args.scale)
+    prob = build_problem(args.seed, torch.device("cpu"), args.scale)
     hp = _host_problem(prob)
-    cfg = describe(prob, args.gpus, gemm="cpu-fp32")
+    cfg = describe(prob, args.gpus, gemm="cpu-fp32", order="CSR row order (C restatement, OpenMP over rows)")
     del prob
-    torch.cuda.empty_cache()
     threads = O.max_threads()
     total = args.steps + args.warmup
     per_step = max(0.5, min(4.0, 150.0 / max(1, total)))  # whole run within a few minutes
@@ -497,7 +675,7 @@ def run_reference(args, device: torch.device):
     return {"metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "fp32", "impl": "reference",
-            "data": f"synthetic: seeded R-MAT graph (seed {args.seed}) with ogbn-products shape",
+            "data": f"synthetic: seeded R-MAT graph (seed {args.seed}) with ogbn-products shape, built on the host",
             "config": cfg,
             "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                              "sample": sample},
@@ -782,7 +960,8 @@ def main() -> int:
     if world != args.gpus:
         log(f"[bench] WORLD_SIZE={world} but --gpus={args.gpus}; using WORLD_SIZE")
     device = torch.device("cuda", local_rank)
-    torch.cuda.set_device(device)
+    if args.impl != "reference":
+        torch.cuda.set_device(device)
     if args.workload == "gin_papers_like":
         if rank != 0:
             return 0
@@ -816,7 +995,7 @@ def main() -> int:
     if args.impl == "reference":
         if rank != 0:
             return 0
-        print(json.dumps(run_reference(args, device)), flush=True)
+        print(json.dumps(run_reference(args)), flush=True)
         return 0
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)

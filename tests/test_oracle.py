@@ -131,3 +131,28 @@ def test_split_rule_segments_and_chunks():
         assert np.array_equal(got.view(np.uint32), acc.view(np.uint32)), warps
         plain = O.spmm(rp, cols, x, mode=O.W_UNIT)[0]
         assert not np.array_equal(plain.view(np.uint32), got.view(np.uint32)) or warps == 0
+
+
+@pytest.mark.parametrize("mode,mean", [(O.W_GCN, O.M_NONE), (O.W_EDGE, O.M_NONE), (O.W_UNIT, O.M_DIV),
+                                       (O.W_UNIT, O.M_RCP)])
+def test_listed_rows_equal_whole_graph_rows(graph, mode, mean):
+    """spmm_rows / spmm_f64_rows on a row list, and the compact sub-problem of
+    sampled rows, reproduce the whole-graph results of those rows exactly."""
+    rp, ci, dis, ew, x = graph
+    rows = np.array([599, 0, 17, 17, 300, 42], dtype=np.int64)
+    kw = dict(mode=mode, dis=dis if mode == O.W_GCN else None, ew=ew if mode == O.W_EDGE else None, mean=mean)
+    whole = O.spmm(rp, ci, x, split_warps=16, long_thr=10, **kw)
+    listed = O.spmm_rows(rp, ci, x, rows, split_warps=16, long_thr=10, **kw)
+    assert np.array_equal(whole[rows].view(np.uint32), listed.view(np.uint32))
+    f64, ab = O.spmm_f64(rp, ci, x, **kw)
+    g64, gab = O.spmm_f64_rows(rp, ci, x, rows, **kw)
+    assert np.array_equal(f64[rows], g64) and np.array_equal(ab[rows], gab)
+    if mode == O.W_EDGE:
+        return  # the compact sub-problem carries row scales (dis), not per-entry weights
+    srp, sci, sx, sdis = O.compact_rows_problem(torch.from_numpy(rp), torch.from_numpy(ci), torch.from_numpy(x),
+                                                rows, torch.from_numpy(dis) if mode == O.W_GCN else None)
+    k = rows.size
+    sub = O.spmm(srp, sci, sx, mode=mode, dis=sdis, mean=mean, split_warps=16, long_thr=10, rows=(0, k))
+    assert np.array_equal(whole[rows].view(np.uint32), sub.view(np.uint32))
+    s64, sab = O.spmm_f64_rows(srp, sci, sx, np.arange(k), mode=mode, dis=sdis, mean=mean)
+    assert np.allclose(s64, f64[rows], rtol=0, atol=0) and np.allclose(sab, ab[rows], rtol=0, atol=0)
