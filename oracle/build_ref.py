@@ -13,7 +13,8 @@ B200 (compute capability 10.0, ``loader.py:42-44``). Nothing is copied into
 this repository; the build products go only to ``oracle/_ref/`` (git-ignored,
 but shipped to the GPU machine with the rest of the tree).
 
-Usage:  python oracle/build_ref.py [--reference /root/reference] [--jobs 3]
+Usage:  python oracle/build_ref.py [--reference DIR] [--jobs 3]
+(DIR defaults to $GNN_REFERENCE_ROOT, else a ``reference`` directory beside this repository.)
 """
 from __future__ import annotations
 
@@ -59,7 +60,7 @@ def _build_one(args: tuple[str, list[str], str]) -> str:
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("GNN_REFERENCE_ROOT", str(HERE.parent.parent / "reference")))
     ap.add_argument("--jobs", type=int, default=3)
     args = ap.parse_args()
     native_dir = Path(args.reference) / "GNN_cuda_common" / "native"

@@ -12,11 +12,12 @@ empty edge list, a power-law graph), the outputs of
 into ``tests/golden/csr_cases.npz``. The tests check both the oracle's
 restatement and this package's builders against these arrays bit for bit.
 
-Usage:  python tests/golden/make_golden.py [--reference /root/reference]
+Usage:  python tests/golden/make_golden.py [--reference DIR]  (default: $GNN_REFERENCE_ROOT, else ../reference)
 """
 from __future__ import annotations
 
 import argparse
+import os
 import importlib.util
 import sys
 from pathlib import Path
@@ -65,7 +66,8 @@ def _cases() -> dict[str, tuple[np.ndarray, np.ndarray, int]]:
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("GNN_REFERENCE_ROOT",
+                    str(Path(__file__).resolve().parents[3] / "reference")))
     args = ap.parse_args()
     gu = _load_reference_graph_utils(Path(args.reference))
     arrays: dict[str, np.ndarray] = {}

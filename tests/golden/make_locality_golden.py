@@ -16,11 +16,12 @@ graph), plus a hot partition without a base order. Everything goes into
 ``tests/golden/locality_cases.npz``; the tests check the oracle's restatement
 (oracle/locality.py) and the device implementation against it bit for bit.
 
-Usage:  python tests/golden/make_locality_golden.py [--reference /root/reference]
+Usage:  python tests/golden/make_locality_golden.py [--reference DIR]  (default: $GNN_REFERENCE_ROOT, else ../reference)
 """
 from __future__ import annotations
 
 import argparse
+import os
 import importlib.util
 import sys
 from pathlib import Path
@@ -124,7 +125,8 @@ def _record_hot(arrays: dict, key: str, hot: dict) -> None:
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("GNN_REFERENCE_ROOT",
+                    str(Path(__file__).resolve().parents[3] / "reference")))
     args = ap.parse_args()
     gu = _load_reference_graph_utils(Path(args.reference))
     arrays: dict[str, np.ndarray] = {}
