@@ -823,15 +823,21 @@ def run_gin(args, device: torch.device) -> dict:
     """gin_inference.py's layer, per layer: sum aggregation, + (1 + eps)·x (eps = 0),
     Linear(128,128)+ReLU, Linear(128,128) (+ReLU between layers) — the reference's
     composition (gin_inference.py:317-359) on this library's kernels. The whole
-    111M-node, 1.6B-entry graph needs X, the aggregate, the hidden and the output
-    matrices (4 x 57 GB) at once, more than one GPU holds; --scale picks the
-    fraction of nodes and entries (default 1/4 for this workload)."""
-    scale = args.scale if args.scale != 1.0 else 0.25
+    111M-node, 1.6B-entry graph (int64 row_ptr) needs X and two output matrices
+    (3 x 57 GB) plus the CSR; the separate calls would add the aggregate and the
+    hidden matrices (2 x 57 GB more), which one GPU does not hold, so at full
+    size every layer runs as one fused kernel (gnn_fused_aggregate_linear: the
+    same results as the separate calls, no [N, F] intermediate). --scale picks
+    a fraction of the nodes and entries; below 1/2 the separate calls run."""
+    from gnn_cuda_b200.GNN_cuda_common import fused_ops
+    scale = args.scale
+    torch.backends.cuda.matmul.allow_tf32 = True
     t0 = time.time()
     src, dst, n = synth.make_graph("gin_papers_like", seed=args.seed, device=device, scale_nodes=scale)
+    full = scale >= 1.0
     nnz_est = int(src.numel())
     rp, ci, _ = synth.csr_on_device(src, dst, n, add_self_loops=False,
-                                    index_dtype=torch.int64 if nnz_est > 2**31 - 1 else torch.int32)
+                                    index_dtype=torch.int64 if (full or nnz_est > 2**31 - 1) else torch.int32)
     del src, dst
     torch.cuda.empty_cache()
     nnz = int(ci.numel())
@@ -839,24 +845,31 @@ def run_gin(args, device: torch.device) -> dict:
     w1 = [synth.glorot(GIN_FEAT, GIN_FEAT, seed=args.seed + 10 + i, device=device) for i in range(GIN_LAYERS)]
     w2 = [synth.glorot(GIN_FEAT, GIN_FEAT, seed=args.seed + 20 + i, device=device) for i in range(GIN_LAYERS)]
     b = [torch.zeros(GIN_FEAT, device=device) for _ in range(GIN_LAYERS)]
-    agg = torch.empty(n, GIN_FEAT, device=device)
-    hid = torch.empty(n, GIN_FEAT, device=device)
+    fused = scale >= 0.5 and fused_ops.fused_supported(GIN_FEAT, GIN_FEAT, GIN_FEAT)
     outs = [torch.empty(n, GIN_FEAT, device=device) for _ in range(2)]
+    if not fused:
+        agg = torch.empty(n, GIN_FEAT, device=device)
+        hid = torch.empty(n, GIN_FEAT, device=device)
     torch.cuda.synchronize(device)
-    log(f"[bench] gin graph n={n} nnz={nnz} built in {time.time() - t0:.1f}s")
-    torch.backends.cuda.matmul.allow_tf32 = True
+    log(f"[bench] gin graph n={n} nnz={nnz} built in {time.time() - t0:.1f}s; "
+        f"{'fused layers' if fused else 'separate calls'}; "
+        f"{torch.cuda.memory_allocated(device) / 1e9:.1f} GB allocated")
     timers: dict = {}
 
     def step(tm=None):
         h = x
         for li in range(GIN_LAYERS):
-            ev = partition._mark(tm, "spmm_begin")
-            agg_ops.spmm_sum_forward_(rp, ci, h, agg)
-            partition._mark(tm, "spmm_end", ev)
-            agg_ops.tensor_add_inplace_(agg, h, 1.0)  # (1 + eps) * x with eps = 0
-            agg_ops.linear_forward_(agg, w1[li], b[li], hid, True)
             o = outs[li % 2]
-            agg_ops.linear_forward_(hid, w2[li], b[li], o, li != GIN_LAYERS - 1)
+            ev = partition._mark(tm, "spmm_begin")
+            if fused:
+                fused_ops.gin_layer_forward_(rp, ci, h, 0.0, w1[li], b[li], w2[li], b[li], o, li != GIN_LAYERS - 1)
+                partition._mark(tm, "spmm_end", ev)
+            else:
+                agg_ops.spmm_sum_forward_(rp, ci, h, agg)
+                partition._mark(tm, "spmm_end", ev)
+                agg_ops.tensor_add_inplace_(agg, h, 1.0)  # (1 + eps) * x with eps = 0
+                agg_ops.linear_forward_(agg, w1[li], b[li], hid, True)
+                agg_ops.linear_forward_(hid, w2[li], b[li], o, li != GIN_LAYERS - 1)
             h = o
         return h
 
@@ -887,10 +900,13 @@ def run_gin(args, device: torch.device) -> dict:
                 "nodes and entries, N(0,1) features, Glorot weights, zero bias",
         "config": {"workload": f"gin_papers_like x{scale:g}: GIN 3 layers, eps = 0, MLP Linear(128,128)-ReLU-"
                                "Linear(128,128), ReLU between layers", "nodes": n, "csr_entries": nnz,
+                   "layer": "fused aggregation + MLP (one kernel per layer)" if fused else "separate calls",
                    "feat_dim": GIN_FEAT, "layers": GIN_LAYERS, "self_loops": False,
                    "row_ptr": "int64" if rp.dtype == torch.int64 else "int32", "row_order": row_order(),
                    "l2": "inputs larger than L2 (X is %.1f GB), no flush" % (n * GIN_FEAT * 4 / 1e9)},
-        "roofline": {"bound": "hbm", "kernel": "spmm_vec_kernel + spmm_long_kernel (sum aggregation)",
+        "roofline": {"bound": "hbm", "kernel": ("fused_layer_kernel + spmm_long_kernel (sum aggregation and MLP; "
+                                                "the time includes the two transforms)") if fused else
+                     "spmm_vec_kernel + spmm_long_kernel (sum aggregation)",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
                      "peak_source": peak_kind, "spmm_ms_per_layer": round(spmm_ms, 4),
                      "algorithmic_bytes_per_layer": bytes_layer, "traffic": None},

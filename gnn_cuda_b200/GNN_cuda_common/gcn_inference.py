@@ -18,7 +18,8 @@ import torch
 
 from . import _driver as D
 from . import native_ops
-from .agg_ops import linear_forward_
+from .agg_ops import bias_relu_forward_, gemm_forward_, linear_forward_
+from .fused_ops import fused_supported, gcn_layer_forward_
 from .allocator import (
     ManagedAllocationConfig,
     allocate_empty,
@@ -60,11 +61,28 @@ def _managed_hints(tensors, cfg: ManagedAllocationConfig, device, *, read_mostly
             prefetch_managed(t, location=cfg.prefetch_to, device=device)
 
 
-def _make_layer_state(in_dim, out_dim, *, num_nodes, device, weight_mode, activation_mode, cfg) -> LayerState:
+def _layer_plan(args, idx: int, in_dim: int, out_dim: int, *, device, impl: str, optimized_first: bool) -> str:
+    """How layer idx runs: "transform_first" (x·W, then aggregate; --layer_order),
+    "fused" (one kernel for the aggregation and the transform; --fuse_layers,
+    supported widths, TF32, the symmetric-normalisation kernels, not the first
+    layer of spmm_mode=optimized) or "aggregate_first" (separate calls)."""
+    if D.transform_first(str(args.layer_order), in_dim, out_dim):
+        return "transform_first"
+    if (bool(args.fuse_layers) and device.type == "cuda" and impl != "pyg_baseline"
+            and not (idx == 0 and optimized_first) and fused_supported(in_dim, out_dim)):
+        return "fused"
+    return "aggregate_first"
+
+
+def _make_layer_state(in_dim, out_dim, *, num_nodes, device, weight_mode, activation_mode, cfg,
+                      plan: str = "aggregate_first") -> LayerState:
     w_cpu, b_cpu = D.init_linear_params(in_dim, out_dim)
     w = allocate_like_mode(w_cpu, memory_mode=weight_mode, device=device)
     b = allocate_like_mode(b_cpu, memory_mode=weight_mode, device=device)
-    agg = allocate_empty((num_nodes, in_dim), dtype=torch.float32, device=device, memory_mode=activation_mode)
+    # the aggregate buffer: [N, in] (aggregate first), [N, out] (x·W first), none when fused
+    agg_rows = 0 if plan == "fused" else num_nodes
+    agg_cols = out_dim if plan == "transform_first" else in_dim
+    agg = allocate_empty((agg_rows, agg_cols), dtype=torch.float32, device=device, memory_mode=activation_mode)
     out = allocate_empty((num_nodes, out_dim), dtype=torch.float32, device=device, memory_mode=activation_mode)
     if is_uvm_mode(weight_mode):
         _managed_hints((w, b), cfg, device, read_mostly=False)
@@ -241,10 +259,13 @@ def run_gcn_inference(*, framework_label: str, select_device: Callable[[str], to
             hot_cache = torch.empty((hot_cutoff, int(features_cpu.size(1))), dtype=torch.float32, device=device)
             optimized_active = True
 
+        dims = D.layer_dims(int(features_cpu.size(1)), int(args.hidden_dim), int(args.out_dim), int(args.num_layers))
+        plans = [_layer_plan(args, idx, i, o, device=device, impl=impl, optimized_first=optimized_active)
+                 for idx, (i, o) in enumerate(dims)]
+        print(f"Layer plan: {', '.join(plans)}")
         layers = [_make_layer_state(i, o, num_nodes=int(num_nodes), device=device, weight_mode=place.weight,
-                                    activation_mode=place.activation, cfg=cfg)
-                  for i, o in D.layer_dims(int(features_cpu.size(1)), int(args.hidden_dim), int(args.out_dim),
-                                           int(args.num_layers))]
+                                    activation_mode=place.activation, cfg=cfg, plan=plan)
+                  for (i, o), plan in zip(dims, plans)]
         if reserve_on:
             # the aggregation's scratch must exist before the reserve takes the free memory
             native_ops.ensure_workspace(device, int(num_nodes), int(col_ind.numel()))
@@ -288,18 +309,24 @@ def run_gcn_inference(*, framework_label: str, select_device: Callable[[str], to
     feature_addr_start = int(features.data_ptr())
     feature_addr_end = feature_addr_start + rs["feature_bytes"]
 
-    def aggregate(layer: LayerState, idx: int, tag: str, mode: str, x: torch.Tensor) -> None:
+    def aggregate(layer: LayerState, idx: int, tag: str, mode: str, x: torch.Tensor,
+                  dst: torch.Tensor | None = None) -> None:
+        dst = layer.agg_buffer if dst is None else dst
         with D.nvtx_range(nvtx, f"{tag}/aggregation"):
             with phases.measure("spmm"):
                 first = idx == 0
-                if impl == "pyg_baseline":
-                    spmm_pyg_gcn_forward_(row_ptr, col_ind, edge_weight, x, layer.agg_buffer, spmm_mode=mode,
+                if plans[idx] == "fused":
+                    # aggregation and transform in one kernel: the layer's output directly
+                    gcn_layer_forward_(row_ptr, col_ind, deg_inv_sqrt, x, layer.weight, layer.bias, layer.out_buffer,
+                                       relu=idx != len(layers) - 1)
+                elif impl == "pyg_baseline":
+                    spmm_pyg_gcn_forward_(row_ptr, col_ind, edge_weight, x, dst, spmm_mode=mode,
                                           optimized_backend=place.ft if first else "hmm",
                                           row_schedule=row_schedule if first else None,
                                           hot_feature_cache=hot_cache if first else None,
                                           hot_node_cutoff=hot_cutoff if first else 0)
                 else:
-                    spmm_gcn_forward_(row_ptr, col_ind, deg_inv_sqrt, x, layer.agg_buffer, spmm_mode=mode,
+                    spmm_gcn_forward_(row_ptr, col_ind, deg_inv_sqrt, x, dst, spmm_mode=mode,
                                       row_schedule=row_schedule if first else None,
                                       hot_feature_cache=hot_cache if first else None,
                                       hot_node_cutoff=hot_cutoff if first else 0)
@@ -313,18 +340,29 @@ def run_gcn_inference(*, framework_label: str, select_device: Callable[[str], to
                 mode = "optimized"
             elif idx != 0 and mode == "optimized":
                 mode = "plain"
+            relu = idx != len(layers) - 1
+            src, dst = x, None
+            if plans[idx] == "transform_first":
+                # A·(x·W): the narrower x·W rows are gathered; bias and ReLU after the aggregation
+                with D.nvtx_range(nvtx, f"{tag}/dense_update"):
+                    with phases.measure("gemm"):
+                        gemm_forward_(x, layer.weight, layer.agg_buffer)
+                src, dst = layer.agg_buffer, layer.out_buffer
             if idx == 0:
                 activate_reserve()
                 try:
-                    aggregate(layer, idx, tag, mode, x)
+                    aggregate(layer, idx, tag, mode, src, dst)
                 finally:
                     release_reserve()
             else:
-                aggregate(layer, idx, tag, mode, x)
-            with D.nvtx_range(nvtx, f"{tag}/dense_update"):
+                aggregate(layer, idx, tag, mode, src, dst)
+            if plans[idx] == "aggregate_first":
+                with D.nvtx_range(nvtx, f"{tag}/dense_update"):
+                    with phases.measure("gemm"):
+                        linear_forward_(layer.agg_buffer, layer.weight, layer.bias, layer.out_buffer, relu=relu)
+            elif plans[idx] == "transform_first":
                 with phases.measure("gemm"):
-                    linear_forward_(layer.agg_buffer, layer.weight, layer.bias, layer.out_buffer,
-                                    relu=idx != len(layers) - 1)
+                    bias_relu_forward_(layer.out_buffer, layer.bias, relu)
             x = layer.out_buffer
         return x
 

@@ -18,7 +18,8 @@ from typing import Callable
 import torch
 
 from . import _driver as D
-from .agg_ops import linear_forward_, spmm_sum_forward_, tensor_add_inplace_
+from .agg_ops import bias_relu_forward_, gemm_forward_, linear_forward_, spmm_sum_forward_, tensor_add_inplace_
+from .fused_ops import fused_supported, gin_layer_forward_
 from .allocator import (
     ManagedAllocationConfig,
     allocate_empty,
@@ -56,18 +57,22 @@ def _apply_policy_if_needed(t, *, memory_mode, cfg, device, read_mostly, prefetc
         prefetch_managed(t, location=cfg.prefetch_to, device=device)
 
 
-def _make_layer_state(in_dim, out_dim, *, num_nodes, device, memory_mode, cfg, learn_eps) -> GINLayerState:
+def _make_layer_state(in_dim, out_dim, *, num_nodes, device, memory_mode, cfg, learn_eps,
+                      plan: str = "aggregate_first") -> GINLayerState:
     w1_cpu, b1_cpu = D.init_linear_params(in_dim, out_dim)
     w2_cpu, b2_cpu = D.init_linear_params(out_dim, out_dim)
     eps_cpu = torch.zeros((1,), dtype=torch.float32)
+    # fused: no aggregate / hidden buffers; x·W1 first: the aggregate buffer holds x·W1 ([N, out])
+    rows = 0 if plan == "fused" else num_nodes
+    agg_cols = out_dim if plan == "transform_first" else in_dim
     st = GINLayerState(
         weight1=allocate_like_mode(w1_cpu, memory_mode=memory_mode, device=device),
         bias1=allocate_like_mode(b1_cpu, memory_mode=memory_mode, device=device),
         weight2=allocate_like_mode(w2_cpu, memory_mode=memory_mode, device=device),
         bias2=allocate_like_mode(b2_cpu, memory_mode=memory_mode, device=device),
         eps=allocate_like_mode(eps_cpu, memory_mode=memory_mode, device=device),
-        agg_buffer=allocate_empty((num_nodes, in_dim), dtype=torch.float32, device=device, memory_mode=memory_mode),
-        hidden_buffer=allocate_empty((num_nodes, out_dim), dtype=torch.float32, device=device, memory_mode=memory_mode),
+        agg_buffer=allocate_empty((rows, agg_cols), dtype=torch.float32, device=device, memory_mode=memory_mode),
+        hidden_buffer=allocate_empty((rows, out_dim), dtype=torch.float32, device=device, memory_mode=memory_mode),
         out_buffer=allocate_empty((num_nodes, out_dim), dtype=torch.float32, device=device, memory_mode=memory_mode))
     if not learn_eps:
         st.eps.requires_grad_(False)
@@ -75,6 +80,16 @@ def _make_layer_state(in_dim, out_dim, *, num_nodes, device, memory_mode, cfg, l
         _apply_policy_if_needed(t, memory_mode=memory_mode, cfg=cfg, device=device, read_mostly=False)
     st.alpha = 1.0 + float(st.eps.item())
     return st
+
+
+def _layer_plan(args, in_dim: int, out_dim: int, *, device) -> str:
+    """"transform_first" (x·W1 before the sum; --layer_order), "fused" (one
+    kernel per layer; --fuse_layers, supported widths, TF32) or "aggregate_first"."""
+    if D.transform_first(str(args.layer_order), in_dim, out_dim):
+        return "transform_first"
+    if bool(args.fuse_layers) and device.type == "cuda" and fused_supported(in_dim, out_dim, out_dim):
+        return "fused"
+    return "aggregate_first"
 
 
 def build_parser():
@@ -129,15 +144,40 @@ def run_gin_inference(*, framework_label: str, select_device: Callable[[str], to
                 if device.type == "cuda":
                     torch.cuda.synchronize(device)
             prefetch_managed(features, location=cfg.prefetch_to, device=device)
+        dims = D.layer_dims(int(features.size(1)), int(args.hidden_dim), int(args.out_dim), int(args.num_layers))
+        plans = [_layer_plan(args, i, o, device=device) for i, o in dims]
+        print(f"Layer plan: {', '.join(plans)}")
         layers = [_make_layer_state(i, o, num_nodes=int(num_nodes), device=device, memory_mode=place.weight, cfg=cfg,
-                                    learn_eps=bool(args.learn_eps))
-                  for i, o in D.layer_dims(int(features.size(1)), int(args.hidden_dim), int(args.out_dim),
-                                           int(args.num_layers))]
+                                    learn_eps=bool(args.learn_eps), plan=plan)
+                  for (i, o), plan in zip(dims, plans)]
 
     def forward_once() -> torch.Tensor:
         x = features
         for idx, layer in enumerate(layers):
             tag = f"layer{idx + 1}"
+            relu_out = post_layer_relu and idx != len(layers) - 1
+            if plans[idx] == "fused":
+                # sum, + (1+eps)·x, Linear-ReLU-Linear in one kernel (same results as the calls below)
+                with D.nvtx_range(nvtx, f"{tag}/fused"):
+                    with phases.measure("spmm"):
+                        gin_layer_forward_(row_ptr, col_ind, x, layer.alpha - 1.0, layer.weight1, layer.bias1,
+                                           layer.weight2, layer.bias2, layer.out_buffer, relu_out)
+                x = layer.out_buffer
+                continue
+            if plans[idx] == "transform_first":
+                # sum and (1+eps)·x are linear: ((1+eps)x + Σx)·W1 = (1+eps)(x·W1) + Σ(x·W1)
+                with phases.measure("gemm"):
+                    gemm_forward_(x, layer.weight1, layer.agg_buffer)
+                with phases.measure("spmm"):
+                    spmm_sum_forward_(row_ptr, col_ind, layer.agg_buffer, layer.hidden_buffer,
+                                      hmm_optimized=use_hmm_spmm)
+                with phases.measure("epilogue"):
+                    tensor_add_inplace_(layer.hidden_buffer, layer.agg_buffer, alpha=layer.alpha)
+                    bias_relu_forward_(layer.hidden_buffer, layer.bias1, True)
+                with phases.measure("gemm"):
+                    linear_forward_(layer.hidden_buffer, layer.weight2, layer.bias2, layer.out_buffer, relu_out)
+                x = layer.out_buffer
+                continue
             with D.nvtx_range(nvtx, f"{tag}/aggregation"):
                 with phases.measure("spmm"):
                     spmm_sum_forward_(row_ptr, col_ind, x, layer.agg_buffer, hmm_optimized=use_hmm_spmm)

@@ -17,7 +17,15 @@ from typing import Callable
 import torch
 
 from . import _driver as D
-from .agg_ops import gemm_forward_, linear_forward_, relu_inplace_, spmm_mean_forward_, tensor_add_inplace_
+from .agg_ops import (
+    bias_relu_forward_,
+    gemm_forward_,
+    linear_forward_,
+    relu_inplace_,
+    spmm_mean_forward_,
+    tensor_add_inplace_,
+)
+from .fused_ops import fused_supported, mean_linear_forward_
 from .allocator import (
     ManagedAllocationConfig,
     allocate_empty,
@@ -53,7 +61,19 @@ def _apply_policy_if_needed(t, *, memory_mode, cfg, device, read_mostly, prefetc
         prefetch_managed(t, location=cfg.prefetch_to, device=device)
 
 
-def _make_layer_state(in_dim, out_dim, *, num_nodes, device, memory_mode, cfg) -> GraphSAGELayerState:
+def _layer_plan(args, in_dim: int, out_dim: int, *, device) -> str:
+    """The neighbour half mean(x)·W_n + b_n: "transform_first" (mean of x·W_n;
+    --layer_order), "fused" (one kernel; --fuse_layers, supported widths, TF32)
+    or "aggregate_first"."""
+    if D.transform_first(str(args.layer_order), in_dim, out_dim):
+        return "transform_first"
+    if bool(args.fuse_layers) and device.type == "cuda" and fused_supported(in_dim, out_dim):
+        return "fused"
+    return "aggregate_first"
+
+
+def _make_layer_state(in_dim, out_dim, *, num_nodes, device, memory_mode, cfg,
+                      plan: str = "aggregate_first") -> GraphSAGELayerState:
     wn_cpu, bn_cpu = D.init_linear_params(in_dim, out_dim, bias=True)
     wr_cpu, _ = D.init_linear_params(in_dim, out_dim, bias=False)
     br_cpu = torch.zeros((out_dim,), dtype=torch.float32)
@@ -62,7 +82,8 @@ def _make_layer_state(in_dim, out_dim, *, num_nodes, device, memory_mode, cfg) -
         bias_neigh=allocate_like_mode(bn_cpu, memory_mode=memory_mode, device=device),
         weight_root=allocate_like_mode(wr_cpu, memory_mode=memory_mode, device=device),
         bias_root=allocate_like_mode(br_cpu, memory_mode=memory_mode, device=device),
-        agg_buffer=allocate_empty((num_nodes, in_dim), dtype=torch.float32, device=device, memory_mode=memory_mode),
+        agg_buffer=allocate_empty((0 if plan == "fused" else num_nodes, out_dim if plan == "transform_first" else in_dim),
+                                  dtype=torch.float32, device=device, memory_mode=memory_mode),
         root_buffer=allocate_empty((num_nodes, out_dim), dtype=torch.float32, device=device, memory_mode=memory_mode),
         out_buffer=allocate_empty((num_nodes, out_dim), dtype=torch.float32, device=device, memory_mode=memory_mode))
     for t in (st.weight_neigh, st.bias_neigh, st.weight_root, st.bias_root, st.agg_buffer, st.root_buffer,
@@ -122,20 +143,41 @@ def run_graphsage_inference(*, framework_label: str, select_device: Callable[[st
                 if device.type == "cuda":
                     torch.cuda.synchronize(device)
             prefetch_managed(features, location=cfg.prefetch_to, device=device)
-        layers = [_make_layer_state(i, o, num_nodes=int(num_nodes), device=device, memory_mode=place.weight, cfg=cfg)
-                  for i, o in D.layer_dims(int(features.size(1)), int(args.hidden_dim), int(args.out_dim),
-                                           int(args.num_layers))]
+        dims = D.layer_dims(int(features.size(1)), int(args.hidden_dim), int(args.out_dim), int(args.num_layers))
+        plans = [_layer_plan(args, i, o, device=device) for i, o in dims]
+        print(f"Layer plan: {', '.join(plans)}")
+        layers = [_make_layer_state(i, o, num_nodes=int(num_nodes), device=device, memory_mode=place.weight, cfg=cfg,
+                                    plan=plan)
+                  for (i, o), plan in zip(dims, plans)]
 
     def forward_once() -> torch.Tensor:
         x = features
         for idx, layer in enumerate(layers):
             tag = f"layer{idx + 1}"
-            with D.nvtx_range(nvtx, f"{tag}/aggregation"):
+            plan = plans[idx]
+            if plan == "fused":
+                # mean aggregation and agg·W_n + b_n in one kernel (same results as the two calls)
+                with D.nvtx_range(nvtx, f"{tag}/fused"):
+                    with phases.measure("spmm"):
+                        mean_linear_forward_(row_ptr, col_ind, x, layer.weight_neigh, layer.bias_neigh,
+                                             layer.out_buffer, False, use_hmm_spmm)
+            elif plan == "transform_first":
+                # mean is linear: mean(x)·W_n = mean(x·W_n), gathering out_dim-wide rows
+                with phases.measure("gemm"):
+                    gemm_forward_(x, layer.weight_neigh, layer.agg_buffer)
                 with phases.measure("spmm"):
-                    spmm_mean_forward_(row_ptr, col_ind, x, layer.agg_buffer, hmm_optimized=use_hmm_spmm)
+                    spmm_mean_forward_(row_ptr, col_ind, layer.agg_buffer, layer.out_buffer, hmm_optimized=use_hmm_spmm)
+                with phases.measure("epilogue"):
+                    bias_relu_forward_(layer.out_buffer, layer.bias_neigh, False)
+            else:
+                with D.nvtx_range(nvtx, f"{tag}/aggregation"):
+                    with phases.measure("spmm"):
+                        spmm_mean_forward_(row_ptr, col_ind, x, layer.agg_buffer, hmm_optimized=use_hmm_spmm)
             with D.nvtx_range(nvtx, f"{tag}/dense_update"):
                 with phases.measure("gemm"):
-                    linear_forward_(layer.agg_buffer, layer.weight_neigh, layer.bias_neigh, layer.out_buffer, False)
+                    if plan == "aggregate_first":
+                        linear_forward_(layer.agg_buffer, layer.weight_neigh, layer.bias_neigh, layer.out_buffer,
+                                        False)
                     gemm_forward_(x, layer.weight_root, layer.root_buffer)
                 with phases.measure("epilogue"):
                     tensor_add_inplace_(layer.out_buffer, layer.root_buffer, alpha=1.0)

@@ -16,6 +16,7 @@ _PKG = Path(__file__).resolve().parent
 LIB_PATH = Path(os.environ.get("GNNB200_LIB", _PKG / "libgnnb200.so"))
 
 GNN_OK = 0
+GNN_AGG_GCN, GNN_AGG_SUM, GNN_AGG_MEAN, GNN_AGG_MEAN_RECIPROCAL = 0, 1, 2, 3
 GNN_INDEX_INT32, GNN_INDEX_INT64 = 0, 1
 GNN_PRECISION_TF32, GNN_PRECISION_FP32 = 0, 1
 
@@ -63,6 +64,10 @@ PROTOTYPES: dict[str, tuple[object, list[object]]] = {
         _i32, [_vp, _i32, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _vp, _sz, _vp]),
     "gnn_spmm_sum_forward": (_i32, [_vp, _i32, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _sz, _vp]),
     "gnn_spmm_mean_forward": (_i32, [_vp, _i32, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _vp, _sz, _vp]),
+    "gnn_fused_layer_supported": (_i32, [_i64, _i64, _i64]),
+    "gnn_fused_aggregate_linear": (
+        _i32, [_vp, _i32, _vp, _vp, _i32, _i64, _vp, _i64, _i64, _i64, _i64, _f32, _i32, _vp, _vp, _i64, _i32, _vp,
+               _vp, _i64, _i32, _vp, _vp, _sz, _vp]),
     "gnn_gemm_forward": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i32, _vp]),
     "gnn_linear_forward": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _i32, _vp]),
     "gnn_bias_relu_forward": (_i32, [_vp, _vp, _i64, _i64, _i32, _vp]),

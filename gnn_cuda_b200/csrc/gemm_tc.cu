@@ -30,9 +30,12 @@
 #include <string>
 
 #include "common.cuh"
+#include "tc_core.cuh"
 
 namespace gnnb200 {
 namespace {
+
+using namespace tc;
 
 constexpr int BM = 128;             // rows per tile (TMEM lanes)
 constexpr int KCHUNK = 32;          // tf32 elements per 128-byte swizzle row
@@ -42,7 +45,6 @@ constexpr int A_STAGE_BYTES = BM * KCHUNK * 4;  // 16 KiB
 constexpr int kThreads = 192;       // warp0 TMA, warp1 MMA/TMEM, warps 2-5 epilogue
 constexpr int OUT_BLOCK_BYTES = 32 * 32 * 4;              // one 32-row x 32-column fp32 output block
 constexpr int OUT_STAGING_BYTES = 4 * 2 * OUT_BLOCK_BYTES;  // 4 epilogue warps x 2 buffers = 32 KiB
-constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 2 GHz
 
 // device status word: 0 ok, otherwise the role that gave up waiting
 __device__ int g_tc_status = 0;
@@ -56,122 +58,6 @@ struct TcParams {
   int relu;
   int stages;  // X chunk ring depth (2..MAX_STAGES)
 };
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-               : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-// Waits for the phase of parity `parity` to complete; false after the deadline.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  const long long t0 = clock64();
-  while (true) {
-    uint32_t done;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(done)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    if (done) return true;
-    if (clock64() - t0 > kWaitCycles) return false;
-  }
-}
-
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
-      ::"r"(smem_u32(dst)), "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
-      : "memory");
-}
-
-// Bulk tensor store of one shared-memory block to global memory (rows past the
-// tensor's extent are clipped by the TMA unit), tracked in this thread's bulk group.
-__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
-  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
-               ::"l"(map), "r"(smem_u32(src)), "r"(x), "r"(y)
-               : "memory");
-}
-__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-// at most one committed store of this thread may still be reading shared memory
-__device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
-// every committed store of this thread has completed
-__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// Shared-memory matrix descriptor, 128-byte swizzle, sm_100 version field = 1.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
-  uint64_t d = 0;
-  d |= static_cast<uint64_t>((addr >> 4) & 0x3FFFu);
-  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
-  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
-  d |= static_cast<uint64_t>(1) << 46;  // descriptor version (sm_100)
-  d |= static_cast<uint64_t>(2) << 61;  // SWIZZLE_128B
-  return d;
-}
-
-// Instruction descriptor: D f32, A/B tf32, both operands K-major, M x N.
-// (An MN-major B operand produced no output for kind::tf32 on B200 in our
-// tests, so W is staged transposed, K-major, instead.)
-__host__ __device__ constexpr uint32_t idesc_tf32(int m, int n) {
-  return (1u << 4) | (2u << 7) | (2u << 10) | (0u << 15) | (0u << 16) |
-         (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
-}
-
-// Byte offset of element (row, k) in a K-major, 128-byte-swizzled operand made of
-// 32-column blocks: block kb = k / 32 holds `rows` rows of 128 B; inside each
-// 1024-byte group of 8 rows, 16-byte chunk c of row r sits at chunk c ^ (r % 8).
-__device__ __forceinline__ uint32_t kmajor_sw128_offset(int row, int k, int rows) {
-  const int kb = k >> 5;
-  const int chunk = (k & 31) >> 2;
-  return static_cast<uint32_t>(kb * rows * 128 + row * 128 + ((chunk ^ (row & 7)) << 4) + ((k & 3) << 2));
-}
-
-__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
-      ::"r"(d_tmem), "l"(a), "l"(b), "r"(idesc), "r"(acc)
-      : "memory");
-}
-
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-
-// Loads 32 consecutive fp32 columns of this thread's TMEM lane. The load and its
-// wait are one asm statement so no use of the registers can be scheduled
-// between the asynchronous load and its completion.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n\t"
-      "tcgen05.wait::ld.sync.aligned;"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr)
-      : "memory");
-}
 
 __device__ __forceinline__ void record_timeout(int code) { atomicCAS(&g_tc_status, 0, code); }
 

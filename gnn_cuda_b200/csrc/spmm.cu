@@ -121,6 +121,7 @@ struct SpmmArgs {
   const int64_t* sched;    // optional row schedule (slot -> row)
   const uint32_t* sched32; // engine-built degree order (slot -> row), per-row kernel only
   float* out;
+  int64_t ldo;             // output row stride in floats (f, or wider when out has more columns)
   int64_t n;
   int64_t f;
   int64_t long_thr;
@@ -406,7 +407,7 @@ __device__ GNN_LONG_PHASE_INLINE void long_rows_phase(const SpmmArgs& a, float4*
       }
       __syncthreads();
     }
-    float4* orow = reinterpret_cast<float4*>(a.out + static_cast<int64_t>(r) * a.f);
+    float4* orow = reinterpret_cast<float4*>(a.out + static_cast<int64_t>(r) * a.ldo);
     for (int j = threadIdx.x; j < 32 * NV; j += blockDim.x) {
       const int64_t cj = static_cast<int64_t>(tile) * kTileF4 + j;
       if (cj < f4) {
@@ -509,7 +510,7 @@ __global__ void __launch_bounds__(kBlockThreads, resident_blocks<NV>())
 #pragma unroll
     for (int q = 0; q < NV; ++q) acc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
     accumulate_edges<WM, HOT, NV, U, IdxT>(a, beg, end, rs, lane, col0, valid, acc, true, c_cur, w_cur);
-    float4* orow = reinterpret_cast<float4*>(a.out + r * a.f);
+    float4* orow = reinterpret_cast<float4*>(a.out + r * a.ldo);
 #pragma unroll
     for (int q = 0; q < NV; ++q) {
       if (valid[q]) st_out_f4(orow + col0 + 32 * q, finish<MEAN>(acc[q], deg));
@@ -597,7 +598,7 @@ __global__ void __launch_bounds__(kBlockThreads, resident_blocks<NV>()) spmm_str
       const int is_live = __shfl_sync(kFull, static_cast<int>(live), cur);
       const int d = __shfl_sync(kFull, true_deg, cur);
       if (is_live) {
-        float4* orow = reinterpret_cast<float4*>(a.out + orow_id * a.f);
+        float4* orow = reinterpret_cast<float4*>(a.out + orow_id * a.ldo);
 #pragma unroll
         for (int q = 0; q < NV; ++q) {
           if (valid[q]) st_out_f4(orow + col0 + 32 * q, finish<MEAN>(acc[q], d));
@@ -763,7 +764,7 @@ __global__ void __launch_bounds__(384, 1) spmm_async_kernel(GNN_KPARAM SpmmArgs 
       const int is_live = __shfl_sync(kFull, static_cast<int>(live), cur);
       const int d = __shfl_sync(kFull, true_deg, cur);
       if (is_live) {
-        float4* orow = reinterpret_cast<float4*>(a.out + orow_id * a.f);
+        float4* orow = reinterpret_cast<float4*>(a.out + orow_id * a.ldo);
 #pragma unroll
         for (int q = 0; q < NV; ++q) {
           if (valid[q]) st_out_f4(orow + col0 + 32 * q, finish<MEAN>(acc[q], d));
@@ -905,7 +906,7 @@ __global__ void __launch_bounds__(256) spmm_scalar_kernel(SpmmArgs a) {
       float v = acc[s];
       if (MEAN == kMeanDiv && deg > 0) v = __fdiv_rn(v, static_cast<float>(deg));
       if (MEAN == kMeanRcp && deg > 0) v = __fmul_rn(v, __fdiv_rn(1.0f, static_cast<float>(deg)));
-      a.out[r * a.f + fi] = v;
+      a.out[r * a.ldo + fi] = v;
     }
   }
 }
@@ -1281,6 +1282,7 @@ int run_typed(const SpmmRequest& q, cudaStream_t stream) {
   a.hot_cutoff = q.hot_cutoff;
   a.sched = q.sched;
   a.out = q.out;
+  a.ldo = q.f;
   a.n = q.n;
   a.f = q.f;
 
@@ -1610,3 +1612,6 @@ extern "C" int gnn_stage_feature_rows(const float* x, int64_t x_rows, float* out
   clear_error();
   return GNN_OK;
 }
+
+// One GNN layer (aggregation + dense transform) in one kernel; shares this file's helpers.
+#include "fused_layer.cuh"

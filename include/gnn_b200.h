@@ -257,6 +257,48 @@ int gnn_tensor_add_inplace(float* dst, const float* src, float alpha, int64_t co
 /* t = max(t, 0) keeping -0 and NaN as they are. Replaces relu_inplace_cuda_, agg_ops.cu:420. */
 int gnn_relu_inplace(float* t, int64_t count, gnn_stream_t stream);
 
+/* ---- one layer in one pass: aggregation + dense transform ------------------- */
+
+/* Aggregations for gnn_fused_aggregate_linear. */
+typedef enum gnn_aggregation {
+  GNN_AGG_GCN = 0,             /* sum of dis[r]·dis[c]·x[c] (spmm_gcn_forward_)                  */
+  GNN_AGG_SUM = 1,             /* sum of x[c] (spmm_sum_forward_)                                  */
+  GNN_AGG_MEAN = 2,            /* sum / deg (spmm_mean_forward_)                                   */
+  GNN_AGG_MEAN_RECIPROCAL = 3  /* sum * (1/deg) (spmm_mean_hmm_forward_)                           */
+} gnn_aggregation;
+
+/* 1 when gnn_fused_aggregate_linear supports these widths on the current
+ * device (sm_100; feat_dim 32, 64, 96 or 128; width1 / width2 32, 64 or 128,
+ * width2 = 0 for a single transform; output width >= feat_dim), else 0. */
+int gnn_fused_layer_supported(int64_t feat_dim, int64_t width1, int64_t width2);
+
+/* One GNN layer without the [N, F] aggregate in device memory:
+ *   a   = aggregate(x) over rows [row_begin, row_begin + num_rows) of the graph
+ *         (GCN / sum / mean, exactly as the aggregation entry points above),
+ *         then a = fma(self_scale, x[row], a) when add_self (GIN's (1+eps)·x);
+ *   h   = relu1?(a · weight1 + bias1)                 weight1 [feat_dim, width1]
+ *   out = relu2?(h · weight2 + bias2)  if width2 > 0  weight2 [width1, width2]
+ *   out = h                            otherwise.
+ * The reference composes each layer from separate calls with an [N, F] buffer
+ * between them: gcn_inference.py:534-600 (spmm_gcn_forward_ -> gemm_forward_ ->
+ * bias_relu_forward_), gin_inference.py:317-359 (spmm_sum_forward_ ->
+ * tensor_add_inplace_ -> linear_forward_ x 2) and the neighbour half of
+ * graphsage_inference.py:310-354. Results are bit-identical to that sequence
+ * on this library's tcgen05 TF32 path (the same row sums and the same MMA
+ * instructions on the same operand bits). x is [num_cols, feat_dim]; out is
+ * [num_rows, width2 ? width2 : width1] and must not alias x; rows above the
+ * long-row threshold are summed into their own row of out first, which is why
+ * the output must be at least feat_dim wide. biases may be NULL; x, out,
+ * weights and biases 16-byte aligned. Workspace:
+ * gnn_spmm_schedule_workspace_bytes(num_rows, num_edges). */
+int gnn_fused_aggregate_linear(const void* row_ptr, int row_ptr_type, const int32_t* col_ind,
+                               const float* deg_inv_sqrt, int aggregation, int64_t row_begin,
+                               const float* x, int64_t num_rows, int64_t num_cols, int64_t num_edges,
+                               int64_t feat_dim, float self_scale, int add_self, const float* weight1,
+                               const float* bias1, int64_t width1, int relu1, const float* weight2,
+                               const float* bias2, int64_t width2, int relu2, float* out,
+                               void* workspace, size_t workspace_bytes, gnn_stream_t stream);
+
 /* ---- unified / host memory (allocator family) ------------------------------ */
 
 /* cudaMallocManaged(bytes, cudaMemAttachGlobal) on `device`; *ptr = NULL for 0 bytes.

@@ -143,6 +143,16 @@ def _gin(graph_dir, post, *extra):
     return cap
 
 
+def _sage(graph_dir, *extra):
+    cap = {}
+    rc = graphsage_inference.run_graphsage_inference(
+        framework_label="pyg", select_device=npz_utils.select_device,
+        load_graph_features=npz_utils.load_pyg_graph_features_from_npz, load_kind="pyg",
+        argv=_argv(graph_dir, *extra), capture=cap)
+    assert rc == 0
+    return cap
+
+
 @pytest.mark.parametrize("post", [False, True])
 def test_gin_fp32_bit_exact(graph_dir, post):
     cap = _gin(graph_dir, post, "--memory_mode", "device", "--no-tf32")
@@ -176,3 +186,29 @@ def test_graphsage_fp32_bit_exact(graph_dir):
         out = O.add_inplace(out, root, np.float32(1.0))
         x = O.relu(out) if li != L - 1 else out
     assert np.array_equal(_np(cap["output"]).view(np.uint32), x.view(np.uint32))
+
+
+def test_fused_layers_equal_separate_calls_in_every_driver(graph_dir):
+    """--fuse_layers (one kernel per layer, no aggregate buffer) returns the same bits
+    as the separate calls on the TF32 path, for GCN, GIN and GraphSAGE-mean."""
+    ref, fused = _gcn(graph_dir), _gcn(graph_dir, "--fuse_layers")
+    assert np.array_equal(_np(fused["output"]).view(np.uint32), _np(ref["output"]).view(np.uint32))
+    assert all(layer.agg_buffer.numel() == 0 for layer in fused["layers"])
+    for post in (False, True):
+        ref, fused = _gin(graph_dir, post), _gin(graph_dir, post, "--fuse_layers")
+        assert np.array_equal(_np(fused["output"]).view(np.uint32), _np(ref["output"]).view(np.uint32))
+    ref, fused = _sage(graph_dir), _sage(graph_dir, "--fuse_layers")
+    assert np.array_equal(_np(fused["output"]).view(np.uint32), _np(ref["output"]).view(np.uint32))
+
+
+def test_transform_first_order_within_tf32_tolerance(graph_dir):
+    """--layer_order transform_first computes A·(x·W): the same layer up to the
+    rounding of a different association, held to the TF32 tolerance of the oracle."""
+    cap = _gcn(graph_dir, "--layer_order", "transform_first")
+    assert _close(_np(cap["output"]), _gcn_oracle(cap, tf32=True), 1e-2)
+    ref = _gin(graph_dir, True)
+    got = _gin(graph_dir, True, "--layer_order", "transform_first")
+    assert _close(_np(got["output"]), _np(ref["output"]).astype(np.float64), 1e-2)
+    ref = _sage(graph_dir)
+    got = _sage(graph_dir, "--layer_order", "transform_first")
+    assert _close(_np(got["output"]), _np(ref["output"]).astype(np.float64), 1e-2)

@@ -67,3 +67,30 @@ def test_phase_summary_cpu_timer():
     assert ps.total_ns("spmm") >= 0.0
     ps.reset()
     assert ps.iteration_values("spmm") == []
+
+
+def test_layer_plan_flags_and_order_rule():
+    """--fuse_layers is off unless asked for; --layer_order auto transforms first
+    exactly when a layer narrows (out_dim < in_dim)."""
+    from gnn_cuda_b200.GNN_cuda_common import _driver as D
+    for mod in (gcn_inference, graphsage_inference, gin_inference):
+        a = mod.build_parser().parse_args([])
+        assert a.fuse_layers is False and a.layer_order == "auto"
+        a = mod.build_parser().parse_args(["--fuse_layers", "--layer_order", "aggregate_first"])
+        assert a.fuse_layers is True and a.layer_order == "aggregate_first"
+    assert D.transform_first("auto", 256, 128) and not D.transform_first("auto", 128, 128)
+    assert not D.transform_first("auto", 128, 256)
+    assert D.transform_first("transform_first", 128, 256) and not D.transform_first("aggregate_first", 256, 64)
+    with pytest.raises(ValueError):
+        D.transform_first("sideways", 1, 1)
+    # on a host without CUDA every layer runs aggregate-first (or transform-first when it narrows)
+    a = gcn_inference.build_parser().parse_args(["--fuse_layers"])
+    cpu = torch.device("cpu")
+    assert gcn_inference._layer_plan(a, 0, 128, 128, device=cpu, impl="legacy_fused",
+                                     optimized_first=False) == "aggregate_first"
+    assert gcn_inference._layer_plan(a, 0, 256, 128, device=cpu, impl="legacy_fused",
+                                     optimized_first=False) == "transform_first"
+    g = gin_inference.build_parser().parse_args(["--fuse_layers"])
+    assert gin_inference._layer_plan(g, 128, 128, device=cpu) == "aggregate_first"
+    s = graphsage_inference.build_parser().parse_args(["--layer_order", "transform_first"])
+    assert graphsage_inference._layer_plan(s, 128, 128, device=cpu) == "transform_first"
