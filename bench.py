@@ -320,6 +320,8 @@ def run_ours(args, rank: int, world: int, device: torch.device):
     # SpMM time per layer on this rank (summed over its row pieces when N > 1)
     spmm_ms = [b.elapsed_time(e) for b, e in timers.get("spmm", [])]
     spmm_ms_avg = sum(spmm_ms) / max(1, args.steps * LAYERS)
+    # exposed exchange: how long the compute stream waits at each layer boundary
+    xchg_ms = sum(b.elapsed_time(e) for b, e in timers.get("xchg", [])) / max(1, args.steps)
 
     # ---- e2e through the public API with host buffers ----
     # every step copies this rank's inputs (its CSR rows, the normalisation vector,
@@ -388,12 +390,31 @@ def run_ours(args, rank: int, world: int, device: torch.device):
     e_end.record(comp)
     torch.cuda.synchronize(device)
     e2e_ms = e_start.elapsed_time(e_end)
+    # the same copies alone (no forward): the host link's share of the end-to-end step
+    copy_ms = None
+    if world == 1:
+        torch.cuda.synchronize(device)
+        c0 = torch.cuda.Event(enable_timing=True)
+        c1 = torch.cuda.Event(enable_timing=True)
+        c0.record(comp)
+        for i in range(args.e2e_steps):
+            s_in.wait_stream(comp)
+            with torch.cuda.stream(s_in):
+                for dst_t, src_t in zip(in_sets[i % len(in_sets)], host_in):
+                    dst_t.copy_(src_t, non_blocking=True)
+            with torch.cuda.stream(s_out):
+                out_host[i % 2].copy_(out_dev[i % 2], non_blocking=True)
+            comp.wait_stream(s_in)
+            comp.wait_stream(s_out)
+        c1.record(comp)
+        torch.cuda.synchronize(device)
+        copy_ms = c0.elapsed_time(c1) / args.e2e_steps
 
     # ---- reduce over ranks ----
     # per-layer algorithmic bytes of this rank's aggregation (its rows, its CSR entries)
     shard_bytes = spmm_layer_bytes(rows, shard.num_edges, FEAT)
-    vals = torch.tensor([ms_total, e2e_ms, spmm_ms_avg, float(launches), float(shard_bytes)], dtype=torch.float64,
-                        device=device)
+    vals = torch.tensor([ms_total, e2e_ms, spmm_ms_avg, float(launches), float(shard_bytes), xchg_ms],
+                        dtype=torch.float64, device=device)
     per_rank = [vals.clone() for _ in range(world)]
     if world > 1:
         dist.all_gather(per_rank, vals)
@@ -437,14 +458,16 @@ def run_ours(args, rank: int, world: int, device: torch.device):
                      "frac_note": "frac = algorithmic bytes / aggregation time / peak (gathered rows served from L2 "
                                   "count too, so it can exceed 1); frac_dram = measured DRAM bytes / the same time / "
                                   "peak",
-                     "spmm_ms_per_rank": [round(float(v), 4) for v in table[:, 2]]},
+                     "spmm_ms_per_rank": [round(float(v), 4) for v in table[:, 2]],
+                     "exchange_wait_ms_per_step_per_rank": [round(float(v), 4) for v in table[:, 5]]},
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h), "ms_per_step": round(e2e_ms / args.e2e_steps, 3),
                 "copies": ("overlapped across steps (two input sets and two output buffers; inputs up / output "
                            "down on two copy streams beside the forward)" if world == 1 else
                            "overlapped across steps (inputs up / output down on two copy streams)") if pipelined
                 else "in step order",
-                "api": "gnn_cuda_b200.GNN_cuda_common.gcn_ops/agg_ops over libgnnb200.so"},
+                "api": "gnn_cuda_b200.GNN_cuda_common.gcn_ops/agg_ops over libgnnb200.so",
+                "copies_only_ms_per_step": round(copy_ms, 3) if copy_ms is not None else None},
         "gpu_launches": int(launches),
         "clocks": clocks.summary(),
     }
@@ -846,6 +869,7 @@ def run_gin(args, device: torch.device) -> dict:
     w2 = [synth.glorot(GIN_FEAT, GIN_FEAT, seed=args.seed + 20 + i, device=device) for i in range(GIN_LAYERS)]
     b = [torch.zeros(GIN_FEAT, device=device) for _ in range(GIN_LAYERS)]
     fused = scale >= 0.5 and fused_ops.fused_supported(GIN_FEAT, GIN_FEAT, GIN_FEAT)
+    torch.cuda.empty_cache()
     outs = [torch.empty(n, GIN_FEAT, device=device) for _ in range(2)]
     if not fused:
         agg = torch.empty(n, GIN_FEAT, device=device)
@@ -990,6 +1014,10 @@ def locality_cpu_baseline(seed: int) -> dict:
 
 def main() -> int:
     args = parse_args()
+    if args.workload == "gin_papers_like":
+        # three 57 GB matrices next to the graph: let the allocator grow segments
+        # instead of failing on fragments left by the graph construction
+        os.environ.setdefault("PYTORCH_CUDA_ALLOC_CONF", "expandable_segments:True")
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

@@ -16,6 +16,8 @@ from typing import Callable
 
 import torch
 
+from .. import _native as N
+from .. import partition
 from . import _driver as D
 from . import native_ops
 from .agg_ops import bias_relu_forward_, gemm_forward_, linear_forward_
@@ -27,6 +29,7 @@ from .allocator import (
     apply_managed_policy,
     is_uvm_mode,
     prefetch_managed,
+    prefetch_rows_in_order,
     uses_cuda_memory_hints,
 )
 from .gcn_ops import spmm_gcn_forward_, stage_feature_rows_
@@ -115,6 +118,11 @@ def build_parser():
     D.add_runtime_flags(p)
     p.add_argument("--ft_host_alloc", type=float, default=0.0,
                    help="target percent of the feature matrix that should not fit in the remaining effective GPU memory")
+    p.add_argument("--prefetch_pieces", type=int, default=0,
+                   help="with --ft_matrix uvm and --prefetch_to cuda: instead of prefetching the features once before "
+                        "the loop, prefetch them in this many row ranges on a side stream in every forward, and run "
+                        "the first aggregation in as many row pieces, piece p starting when range p has arrived "
+                        "(0: the reference's prefetch before the loop)")
     return p
 
 
@@ -196,6 +204,13 @@ def run_gcn_inference(*, framework_label: str, select_device: Callable[[str], to
         if device.type == "cuda":
             torch.cuda.empty_cache()
             torch.cuda.synchronize(device)
+
+    overlap_pieces = int(args.prefetch_pieces)
+    if overlap_pieces < 0:
+        raise ValueError("--prefetch_pieces expects a value >= 0")
+    if overlap_pieces and not (device.type == "cuda" and uses_cuda_memory_hints(place.ft)
+                               and cfg.prefetch_to == "cuda" and impl != "pyg_baseline"):
+        overlap_pieces = 0  # only for unified-memory features prefetched to the GPU
 
     with phases.measure("graph_prep", use_cuda_events=False):
         graph_path = resolve_dataset_path(str(args.dataset), data_root=str(args.data_root))
@@ -294,17 +309,52 @@ def run_gcn_inference(*, framework_label: str, select_device: Callable[[str], to
                 if device.type == "cuda":
                     torch.cuda.synchronize(device)
             if cfg.prefetch_to == "cuda":
-                if reserve_on:
-                    prefetch_managed(features, location=cfg.prefetch_to, device=device, nbytes=rs["prefetch"])
-                else:
+                if not reserve_on:
                     rs["prefetch"] = rs["feature_bytes"]
-                    prefetch_managed(features, location=cfg.prefetch_to, device=device)
+                if overlap_pieces == 0:
+                    prefetch_managed(features, location=cfg.prefetch_to, device=device,
+                                     nbytes=rs["prefetch"] if reserve_on else None)
             else:
                 prefetch_managed(features, location=cfg.prefetch_to, device=device)
         if hot_cache is not None:
             stage_feature_rows_(features, hot_cache)
         if optimized_active:
             spmm_kernel = f"optimized_pyg_{place.ft}" if impl == "pyg_baseline" else f"optimized_{place.ft}"
+
+    # overlapped prefetch: row ranges of the features (the part that is prefetched)
+    # and equal-entry row pieces of the first aggregation
+    pieces, feat_ranges, piece_thr, pf_stream = [], [], 0, None
+    if overlap_pieces and not (optimized_active or plans[0] != "aggregate_first"):
+        row_bytes = int(features.size(1)) * features.element_size()
+        prefix_rows = min(int(num_nodes), int(rs["prefetch"]) // max(1, row_bytes))
+        step = -(-prefix_rows // overlap_pieces) if prefix_rows else 0
+        feat_ranges = [(min(i * step, prefix_rows), min((i + 1) * step, prefix_rows)) for i in range(overlap_pieces)]
+        bounds = partition.piece_bounds(row_ptr.to(torch.int64).cpu().numpy(), overlap_pieces)
+        pieces = [partition.make_shard(row_ptr, col_ind, b0, b1) for b0, b1 in zip(bounds[:-1], bounds[1:])]
+        piece_thr = int(N.lib().gnn_spmm_long_row_threshold(int(num_nodes), int(col_ind.numel())))
+        pf_stream = torch.cuda.Stream(device)
+        print(f"Overlapped prefetch: {len(feat_ranges)} feature ranges of {step} rows, {len(pieces)} row pieces")
+
+    def aggregate_in_pieces(layer: LayerState, tag: str, x: torch.Tensor) -> None:
+        """The first aggregation in row pieces, each waiting only for its feature range."""
+        cur = torch.cuda.current_stream(device)
+        pf_stream.wait_stream(cur)
+        events = prefetch_rows_in_order(x, device=device, row_bounds=[r for r in feat_ranges if r[1] > r[0]],
+                                        stream=pf_stream)
+        old_thr = N.config_get("spmm.long_row_threshold")
+        N.config_set("spmm.long_row_threshold", piece_thr)  # cut long rows as one whole-graph call does
+        try:
+            with D.nvtx_range(nvtx, f"{tag}/aggregation"):
+                with phases.measure("spmm"):
+                    for p_i, shard in enumerate(pieces):
+                        if events:
+                            cur.wait_event(events[min(p_i, len(events) - 1)])
+                        partition.spmm_gcn_shard(shard, deg_inv_sqrt, x,
+                                                 layer.agg_buffer[shard.row_begin:shard.row_end])
+            if events:
+                cur.wait_event(events[-1])
+        finally:
+            N.config_set("spmm.long_row_threshold", old_thr)
 
     feature_addr_start = int(features.data_ptr())
     feature_addr_end = feature_addr_start + rs["feature_bytes"]
@@ -351,7 +401,10 @@ def run_gcn_inference(*, framework_label: str, select_device: Callable[[str], to
             if idx == 0:
                 activate_reserve()
                 try:
-                    aggregate(layer, idx, tag, mode, src, dst)
+                    if pieces:
+                        aggregate_in_pieces(layer, tag, src)
+                    else:
+                        aggregate(layer, idx, tag, mode, src, dst)
                 finally:
                     release_reserve()
             else:

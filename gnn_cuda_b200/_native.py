@@ -49,6 +49,7 @@ PROTOTYPES: dict[str, tuple[object, list[object]]] = {
     "gnn_device_status": (_i32, [_i32, ctypes.POINTER(_i32)]),
     "gnn_spmm_workspace_bytes": (_sz, [_i64, _i64]),
     "gnn_spmm_schedule_workspace_bytes": (_sz, [_i64, _i64]),
+    "gnn_spmm_long_row_threshold": (_i64, [_i64, _i64]),
     "gnn_spmm_gcn_partition_forward": (
         _i32, [_vp, _i32, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _sz, _vp]),
     "gnn_spmm_gcn_forward": (_i32, [_vp, _i32, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _sz, _vp]),

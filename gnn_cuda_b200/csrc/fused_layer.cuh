@@ -43,12 +43,15 @@ namespace gnnb200 {
 namespace {
 
 #ifndef GNN_FUSED_U
-#define GNN_FUSED_U 8  // neighbour rows in flight per gather warp
+// neighbour rows in flight per gather warp. Measured on B200 (GCN layer of the
+// 2.45M-node products-shaped graph): 4 rows 7.4 ms, 8 rows 7.7 ms; rows of up
+// to 32 entries interleaved four at a time (8 or 16 in flight) 9.0-9.7 ms.
+#define GNN_FUSED_U 4
 #endif
 constexpr int kFzGather = 16;                    // gather warps
-constexpr int kFzMmaWarp = kFzGather;            // MMA issue + TMEM allocation
-constexpr int kFzEpi0 = kFzGather + 1;           // first of the four epilogue warps
-constexpr int kFzThreads = (kFzGather + 5) * 32;  // 672
+constexpr int kFzMmaWarp = 0;                    // the gather warp that also issues the MMAs and owns TMEM
+constexpr int kFzEpi0 = kFzGather;               // first of the four epilogue warps
+constexpr int kFzThreads = (kFzGather + 4) * 32;  // 640: 20 warps, 96 registers per thread
 constexpr int kFzBM = 128;                       // tile rows = TMEM lanes = MMA M
 constexpr int kFzRowsPerWarp = kFzBM / kFzGather;
 constexpr int kFzStaging = 4 * 32 * 128;         // per epilogue warp: 32 rows x 128 B
@@ -82,6 +85,110 @@ __device__ __forceinline__ float4 relu4(float4 v) {
   v.z = v.z < 0.0f ? 0.0f : v.z;
   v.w = v.w < 0.0f ? 0.0f : v.w;
   return v;
+}
+
+// The warp's eight rows of the tile, one at a time, exactly as spmm_vec_kernel
+// sums them (32-edge chunks, GNN_FUSED_U neighbour rows in flight, the next
+// row's first chunk of columns loaded while the current row is gathered).
+template <int WM, int MEAN, class IdxT>
+__device__ __forceinline__ void gather_rows_one_by_one(const FusedArgs& p, int lane, int warp, int my_row,
+                                                       IdxT my_beg, IdxT my_end, float my_rs, bool valid_lane,
+                                                       uint8_t* sA) {
+  const SpmmArgs& a = p.a;
+  const int K = static_cast<int>(a.f);
+  const int64_t col0 = lane;
+  const bool valid[1] = {valid_lane};
+  auto first_chunk = [&](int i, int& c, float& w) {
+    const IdxT beg = __shfl_sync(kFull, my_beg, i);
+    const IdxT end = __shfl_sync(kFull, my_end, i);
+    const float rs = __shfl_sync(kFull, my_rs, i);
+    const int64_t deg = static_cast<int64_t>(end - beg);
+    c = 0;
+    w = 0.0f;
+    if (lane < deg) {
+      c = ld_stream_i32(a.col + beg + lane);
+      w = edge_weight<WM>(a, rs, c, static_cast<int64_t>(beg) + lane);
+    }
+  };
+  int c_next = 0;
+  float w_next = 0.0f;
+  first_chunk(0, c_next, w_next);
+#pragma unroll 1
+  for (int i = 0; i < kFzRowsPerWarp; ++i) {
+    const int r = __shfl_sync(kFull, my_row, i);
+    const IdxT beg = __shfl_sync(kFull, my_beg, i);
+    const IdxT end = __shfl_sync(kFull, my_end, i);
+    const float rs = __shfl_sync(kFull, my_rs, i);
+    const int c_cur = c_next;
+    const float w_cur = w_next;
+    if (i + 1 < kFzRowsPerWarp) first_chunk(i + 1, c_next, w_next);
+    float4 acc[1] = {make_float4(0.f, 0.f, 0.f, 0.f)};
+    if (r >= 0) {
+      accumulate_edges<WM, false, 1, GNN_FUSED_U, IdxT>(a, beg, end, rs, lane, col0, valid, acc, true, c_cur, w_cur);
+      acc[0] = finish<MEAN>(acc[0], static_cast<int64_t>(end - beg));
+      if (p.has_self && valid_lane) {
+        const float4 xv =
+            ldg_f4(reinterpret_cast<const float4*>(a.x + (p.x_row0 + static_cast<int64_t>(r)) * K) + col0);
+        acc[0] = fma4(p.self_scale, xv, acc[0]);
+      }
+    }
+    if (valid_lane) *reinterpret_cast<float4*>(sA + tc::kmajor_sw128_offset(warp + i * kFzGather, 4 * lane, kFzBM)) = acc[0];
+  }
+}
+
+// Issues the MMAs of one tile (one thread): the tile times W1 into an
+// accumulator, and with two transforms, once the epilogue has written the
+// hidden tile back over sA, the hidden tile times W2. Returns false after a
+// wait ran out. The instruction sequence is the standalone GEMM's.
+template <bool TWO>
+__device__ __forceinline__ bool fz_issue_mma(uint32_t tmem_base, uint32_t sa, uint32_t sw1, uint32_t sw2, int K,
+                                             int n1, int n2, uint64_t* a_free, uint64_t* acc_full,
+                                             uint64_t* acc_empty, uint64_t* h_full, int buf,
+                                             uint32_t (&empty_phase)[2], uint32_t& h_phase) {
+  using namespace tc;
+  if constexpr (!TWO) {
+    // the epilogue has drained this accumulator (two accumulators alternate)
+    if (!mbar_wait(&acc_empty[buf], empty_phase[buf] ^ 1)) return false;
+    empty_phase[buf] ^= 1;
+  }
+  // (with two transforms accumulator 0 is free: the epilogue read it before the
+  // hidden tile was complete, and this tile was gathered after that)
+  tc_fence_after();
+  const uint32_t idesc1 = idesc_tf32(kFzBM, n1);
+  const uint32_t d1 = tmem_base + static_cast<uint32_t>(buf * 128);
+  for (int kc = 0; kc < K / 32; ++kc) {
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      const uint64_t ad = sw128_desc(sa + kc * (kFzBM * 128) + kk * 32, 16, 1024);
+      const uint64_t bd = sw128_desc(sw1 + kc * (n1 * 128) + kk * 32, 16, 1024);
+      mma_tf32(d1, ad, bd, idesc1, (kc | kk) != 0 ? 1u : 0u);
+    }
+  }
+  if constexpr (!TWO) {
+    mma_commit(a_free);
+    mma_commit(&acc_full[buf]);
+    return true;
+  } else {
+    mma_commit(&acc_full[0]);
+    if (!mbar_wait(h_full, h_phase)) return false;
+    h_phase ^= 1;
+    if (!mbar_wait(&acc_empty[1], empty_phase[1] ^ 1)) return false;
+    empty_phase[1] ^= 1;
+    tc_fence_after();
+    const uint32_t idesc2 = idesc_tf32(kFzBM, n2);
+    const uint32_t d2 = tmem_base + 128u;
+    for (int kc = 0; kc < n1 / 32; ++kc) {
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const uint64_t ad = sw128_desc(sa + kc * (kFzBM * 128) + kk * 32, 16, 1024);
+        const uint64_t bd = sw128_desc(sw2 + kc * (n2 * 128) + kk * 32, 16, 1024);
+        mma_tf32(d2, ad, bd, idesc2, (kc | kk) != 0 ? 1u : 0u);
+      }
+    }
+    mma_commit(a_free);
+    mma_commit(&acc_full[1]);
+    return true;
+  }
 }
 
 template <int WM, int MEAN, class IdxT, bool TWO>
@@ -156,12 +263,15 @@ __global__ void __launch_bounds__(kFzThreads, 1)
 
   if (warp < kFzGather) {
     // ---------------- gather warps: build the aggregate tile ----------------
-    constexpr int U = GNN_FUSED_U;
     const IdxT* __restrict__ rp = static_cast<const IdxT*>(a.row_ptr);
-    const int64_t f4 = K >> 2;
     const int64_t col0 = lane;  // this lane's float4 column (K <= 128: one per lane)
-    const bool valid[1] = {col0 < f4};
+    const bool valid = col0 < (K >> 2);
     uint32_t free_phase = 0;
+    // warp 0, lane 0 also issues the tile's MMAs (its own state)
+    const uint32_t sa = smem_u32(sA), sw1 = smem_u32(sW1), sw2 = smem_u32(sW2);
+    uint32_t full_phase = 0, h_phase = 0;
+    uint32_t empty_phase[2] = {0, 0};
+    int buf = 0;
     for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
       // the previous tile's MMAs have read sA (warp-uniform decision: shuffles follow)
       if (!__all_sync(kFull, mbar_wait(a_free, free_phase ^ 1))) {
@@ -185,122 +295,54 @@ __global__ void __launch_bounds__(kFzThreads, 1)
           }
         }
       }
-      auto first_chunk = [&](int i, int& c, float& w) {
-        const IdxT beg = __shfl_sync(kFull, my_beg, i);
-        const IdxT end = __shfl_sync(kFull, my_end, i);
-        const float rs = __shfl_sync(kFull, my_rs, i);
-        const int64_t deg = static_cast<int64_t>(end - beg);
-        c = 0;
-        w = 0.0f;
-        if (lane < deg) {
-          c = ld_stream_i32(a.col + beg + lane);
-          w = edge_weight<WM>(a, rs, c, static_cast<int64_t>(beg) + lane);
-        }
-      };
-      int c_next = 0;
-      float w_next = 0.0f;
-      if (!p.copy) first_chunk(0, c_next, w_next);
+      if (!p.copy) {
+        gather_rows_one_by_one<WM, MEAN, IdxT>(p, lane, warp, my_row, my_beg, my_end, my_rs, valid, sA);
+      } else {
+        // the rows were summed beforehand into their own rows of out
 #pragma unroll 1
-      for (int i = 0; i < kFzRowsPerWarp; ++i) {
-        const int tr = warp + i * kFzGather;  // tile row
-        const int r = __shfl_sync(kFull, my_row, i);
-        float4 acc[1] = {make_float4(0.f, 0.f, 0.f, 0.f)};
-        if (p.copy) {
-          if (r >= 0 && valid[0]) acc[0] = __ldcg(reinterpret_cast<const float4*>(p.out + static_cast<int64_t>(r) * p.ldo) + col0);
-        } else {
-          const IdxT beg = __shfl_sync(kFull, my_beg, i);
-          const IdxT end = __shfl_sync(kFull, my_end, i);
-          const float rs = __shfl_sync(kFull, my_rs, i);
-          const int c_cur = c_next;
-          const float w_cur = w_next;
-          if (i + 1 < kFzRowsPerWarp) first_chunk(i + 1, c_next, w_next);
-          if (r >= 0) {
-            accumulate_edges<WM, false, 1, U, IdxT>(a, beg, end, rs, lane, col0, valid, acc, true, c_cur, w_cur);
-            acc[0] = finish<MEAN>(acc[0], static_cast<int64_t>(end - beg));
+        for (int i = 0; i < kFzRowsPerWarp; ++i) {
+          const int tr = warp + i * kFzGather;  // tile row
+          const int r = __shfl_sync(kFull, my_row, i);
+          float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (r >= 0 && valid) {
+            v = __ldcg(reinterpret_cast<const float4*>(p.out + static_cast<int64_t>(r) * p.ldo) + col0);
+            if (p.has_self) {
+              const float4 xv =
+                  ldg_f4(reinterpret_cast<const float4*>(a.x + (p.x_row0 + static_cast<int64_t>(r)) * K) + col0);
+              v = fma4(p.self_scale, xv, v);
+            }
           }
+          if (valid) *reinterpret_cast<float4*>(sA + kmajor_sw128_offset(tr, 4 * lane, kFzBM)) = v;
         }
-        if (p.has_self && r >= 0 && valid[0]) {
-          const float4 xv =
-              ldg_f4(reinterpret_cast<const float4*>(a.x + (p.x_row0 + static_cast<int64_t>(r)) * K) + col0);
-          acc[0] = fma4(p.self_scale, xv, acc[0]);
-        }
-        if (valid[0]) *reinterpret_cast<float4*>(sA + kmajor_sw128_offset(tr, 4 * lane, kFzBM)) = acc[0];
       }
       // generic-proxy shared writes -> visible to the tensor core (async proxy)
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(a_full);
-    }
-  } else if (warp == kFzMmaWarp) {
-    // ---------------- MMA issue ----------------
-    if (lane == 0) {
-      const uint32_t sa = smem_u32(sA), sw1 = smem_u32(sW1), sw2 = smem_u32(sW2);
-      const uint32_t idesc1 = idesc_tf32(kFzBM, n1);
-      const uint32_t idesc2 = TWO ? idesc_tf32(kFzBM, n2) : 0u;
-      uint32_t full_phase = 0, h_phase = 0;
-      uint32_t empty_phase[2] = {0, 0};
-      int acc = 0;
-      for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
-        if (!mbar_wait(a_full, full_phase)) {
-          fz_fail();
-          break;
+      if (warp == kFzMmaWarp) {
+        // every gather warp waits for this tile's MMAs (a_free) before the next
+        // tile anyway, so issuing them from here costs no gather time
+        int ok = 1;
+        if (lane == 0) {
+          ok = mbar_wait(a_full, full_phase) ? 1 : 0;
+          full_phase ^= 1;
+          if (ok) {
+            ok = fz_issue_mma<TWO>(tmem_base, sa, sw1, sw2, K, n1, n2, a_free, acc_full, acc_empty, h_full, buf,
+                                   empty_phase, h_phase) ? 1 : 0;
+          }
+          if (!ok) fz_fail();
         }
-        full_phase ^= 1;
-        const int buf = TWO ? 0 : acc;
-        if constexpr (!TWO) {
-          // the epilogue has drained this accumulator (two accumulators alternate)
-          if (!mbar_wait(&acc_empty[buf], empty_phase[buf] ^ 1)) {
-            fz_fail();
-            break;
-          }
-          empty_phase[buf] ^= 1;
-        }
-        // (with two transforms accumulator 0 is free: the epilogue read it before
-        // the hidden tile was complete, and this tile's rows were gathered after that)
-        tc_fence_after();
-        const uint32_t d1 = tmem_base + static_cast<uint32_t>(buf * 128);
-        for (int kc = 0; kc < K / 32; ++kc) {
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t ad = sw128_desc(sa + kc * (kFzBM * 128) + kk * 32, 16, 1024);
-            const uint64_t bd = sw128_desc(sw1 + kc * (n1 * 128) + kk * 32, 16, 1024);
-            mma_tf32(d1, ad, bd, idesc1, (kc | kk) != 0 ? 1u : 0u);
-          }
-        }
-        if constexpr (!TWO) {
-          mma_commit(a_free);
-          mma_commit(&acc_full[buf]);
-          acc ^= 1;
-        } else {
-          mma_commit(&acc_full[0]);
-          // the epilogue turns accumulator 0 into the hidden tile, written over sA
-          if (!mbar_wait(h_full, h_phase)) {
-            fz_fail();
-            break;
-          }
-          h_phase ^= 1;
-          if (!mbar_wait(&acc_empty[1], empty_phase[1] ^ 1)) {
-            fz_fail();
-            break;
-          }
-          empty_phase[1] ^= 1;
-          tc_fence_after();
-          const uint32_t d2 = tmem_base + 128u;
-          for (int kc = 0; kc < n1 / 32; ++kc) {
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-              const uint64_t ad = sw128_desc(sa + kc * (kFzBM * 128) + kk * 32, 16, 1024);
-              const uint64_t bd = sw128_desc(sw2 + kc * (n2 * 128) + kk * 32, 16, 1024);
-              mma_tf32(d2, ad, bd, idesc2, (kc | kk) != 0 ? 1u : 0u);
-            }
-          }
-          mma_commit(a_free);
-          mma_commit(&acc_full[1]);
-        }
+        if (!__shfl_sync(kFull, ok, 0)) break;
+        if constexpr (!TWO) buf ^= 1;
       }
+    }
+    if (warp == kFzMmaWarp) {
       // every MMA issued here completes before TMEM is released
-      mma_commit(drain);
-      if (!mbar_wait(drain, 0)) fz_fail();
+      if (lane == 0) {
+        mma_commit(drain);
+        if (!mbar_wait(drain, 0)) fz_fail();
+      }
+      __syncwarp();
     }
   } else {
     // ---------------- epilogue warps ----------------

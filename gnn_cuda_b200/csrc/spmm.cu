@@ -1438,6 +1438,11 @@ extern "C" size_t gnn_spmm_workspace_bytes(int64_t num_nodes, int64_t num_edges)
   return ws_layout(num_nodes, num_edges).total;
 }
 
+extern "C" int64_t gnn_spmm_long_row_threshold(int64_t num_nodes, int64_t num_edges) {
+  if (num_nodes <= 0 || num_edges < 0) return kMinLongThreshold;
+  return std::min<int64_t>(resolve_long_threshold(num_nodes, num_edges), int64_t(1) << 25);
+}
+
 extern "C" size_t gnn_spmm_schedule_workspace_bytes(int64_t num_nodes, int64_t num_edges) {
   if (num_nodes <= 0 || num_edges < 0) return kWsHeader;
   return ws_layout(num_nodes, num_edges).total + sched_bytes(num_nodes);

@@ -593,18 +593,22 @@ def gcn_forward_push(shard: PaddedShard, dis_pad: torch.Tensor, x_pad: torch.Ten
                 else:
                     exchange.push_rows(halo.ids[c], halo.offsets[c], halo.peers, ready)
         if not last:
+            ev = _mark(timers, "xchg_begin")
             h = exchange.finish()
+            _mark(timers, "xchg_end", ev, series="xchg")
     return out[:shard.num_rows]
 
 
-def _mark(timers: dict | None, key: str, begin=None):
-    """Record a CUDA event for per-kernel timing (key 'spmm_begin' / 'spmm_end').
+def _mark(timers: dict | None, key: str, begin=None, *, series: str = "spmm"):
+    """Record a CUDA event on the current stream for per-phase timing.
 
-    With several pieces per layer, each piece's aggregation is one entry."""
+    With `begin`, the (begin, end) pair is appended to timers[series] ("spmm":
+    one entry per aggregation piece; "xchg": the wait for a layer-boundary
+    exchange to complete, as the compute stream sees it)."""
     if timers is None:
         return None
     ev = torch.cuda.Event(enable_timing=True)
     ev.record()
     if begin is not None:
-        timers.setdefault("spmm", []).append((begin, ev))
+        timers.setdefault(series, []).append((begin, ev))
     return ev

@@ -117,6 +117,14 @@ size_t gnn_spmm_workspace_bytes(int64_t num_nodes, int64_t num_edges);
  * in id order. */
 size_t gnn_spmm_schedule_workspace_bytes(int64_t num_nodes, int64_t num_edges);
 
+/* The degree above which a row of a graph with these sizes is summed in
+ * segments (the "spmm.long_row_threshold" knob when set, else the automatic
+ * value clamp(num_edges / (SMs * 256), 256, 8192) on the current device). A
+ * caller that aggregates a graph in several row pieces sets this value as the
+ * knob so that every piece cuts its rows exactly as one whole-graph call
+ * would. No counterpart in the reference (its kernels never split a row). */
+int64_t gnn_spmm_long_row_threshold(int64_t num_nodes, int64_t num_edges);
+
 /* GCN normalised aggregation, w_e = deg_inv_sqrt[r] * deg_inv_sqrt[col].
  * Replaces spmm_gcn_forward_cuda_ (naive), GNN_cuda_common/native/gcn_ops.cu:327. */
 int gnn_spmm_gcn_forward(const void* row_ptr, int row_ptr_type, const int32_t* col_ind,

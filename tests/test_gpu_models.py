@@ -212,3 +212,13 @@ def test_transform_first_order_within_tf32_tolerance(graph_dir):
     ref = _sage(graph_dir)
     got = _sage(graph_dir, "--layer_order", "transform_first")
     assert _close(_np(got["output"]), _np(ref["output"]).astype(np.float64), 1e-2)
+
+
+def test_overlapped_prefetch_same_bits(graph_dir):
+    """--prefetch_pieces: unified-memory features prefetched in row ranges on a side
+    stream during the forward, the first aggregation in row pieces that wait only
+    for their range — the same output bits as the prefetch before the loop."""
+    base = ("--ft_matrix", "uvm", "--prefetch_to", "cuda", "--preferred_location", "cuda")
+    ref = _gcn(graph_dir, *base)
+    got = _gcn(graph_dir, *base, "--prefetch_pieces", "4")
+    assert np.array_equal(_np(got["output"]).view(np.uint32), _np(ref["output"]).view(np.uint32))

@@ -7,7 +7,7 @@ kernel and by copy engines, and halo pushes of only the rows each peer reads
 halo push skips hold stale values that must never be read) — on contiguous
 row ranges and on rows dealt to ranks by cost, with 1 to 3 pieces per rank.
 
-Runs only where at least two GPUs are visible (spawned ranks, one GPU each,
+Runs on 2 and on 4 GPUs where that many are visible (spawned ranks, one GPU each,
 NCCL with NVLS off). The long-row threshold is fixed so every rank uses the
 same per-row schedule as the single-GPU run.
 """
@@ -99,9 +99,10 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_two_gpu_partitioned_gcn_matches_single_gpu():
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+@pytest.mark.parametrize("world", [2, 4])
+def test_partitioned_gcn_matches_single_gpu(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     from gnn_cuda_b200 import _native as N
     from gnn_cuda_b200.GNN_cuda_common import agg_ops, gcn_ops
     dev = torch.device("cuda", 0)
@@ -123,17 +124,17 @@ def test_two_gpu_partitioned_gcn_matches_single_gpu():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     results = {}
-    for _ in range(2):
+    for _ in range(world):
         r, bcast, padded = q.get(timeout=300)
         results[r] = (bcast, padded)
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    for r in range(2):
+    for r in range(world):
         assert np.array_equal(results[r][0].view(np.uint32), single.view(np.uint32)), ("broadcast", r)
         for k, got in enumerate(results[r][1]):
             assert np.array_equal(got.view(np.uint32), single.view(np.uint32)), ("allgather", k, r)

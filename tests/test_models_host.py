@@ -11,6 +11,7 @@ def test_gcn_flag_defaults_match_reference():
     assert (a.dataset, a.dim, a.num_layers, a.memory_mode, a.spmm_mode, a.gcn_kernel_impl) == \
         ("cora", 128, 2, "uvm", "plain", "legacy_fused")
     assert (a.warmup, a.iters, a.device, a.tf32, a.ft_host_alloc, a.prefetch_to) == (1, 5, "cuda:0", True, 0.0, "none")
+    assert a.prefetch_pieces == 0  # the reference's prefetch before the loop
     assert a.preprocess_meta == "none" and a.pretouch_passes == 0 and a.hmm_mode == "plain"
     a = gcn_inference.build_parser().parse_args(["--no-tf32", "--activation", "device", "--spmm_mode", "optimized"])
     assert a.tf32 is False and a.activation == "device" and a.spmm_mode == "optimized"
