@@ -109,3 +109,68 @@ class UMProfiler:
         _check(lib().gnn_um_profiler_totals(int(lo), int(hi), int(t0), int(t1), ctypes.byref(out)),
                "gnn_um_profiler_totals")
         return {name: getattr(out, name) for name, _ in gnn_um_totals._fields_}
+
+
+class PcieSampler:
+    """Host-link bytes of one GPU over a time window, from NVML's PCIe throughput
+    counters (KB/s over 20 ms windows, sampled every `period_s` and integrated).
+
+    The fallback where CUPTI's unified-memory counters are unavailable (no
+    /dev/nvidia-uvm-tools): during an aggregation over unified-memory features
+    the host-to-device traffic is the feature migration, so the RX bytes stand in
+    for the reference's HtoD_bytes — of the whole device rather than of the
+    feature range, and without a page-fault count. `read` may be replaced (tests)
+    by any callable returning (rx_kb_per_s, tx_kb_per_s)."""
+
+    def __init__(self, device_index: int = 0, period_s: float = 0.02, read=None):
+        self.period_s = float(period_s)
+        self._read = read
+        self._dev = int(device_index)
+        self._stop = threading.Event()
+        self._thread = None
+        self.rx_bytes = 0.0
+        self.tx_bytes = 0.0
+        self.samples = 0
+
+    def _nvml_reader(self):
+        import pynvml
+        pynvml.nvmlInit()
+        handle = None
+        try:
+            import torch
+            props = torch.cuda.get_device_properties(self._dev)
+            bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+            handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            handle = pynvml.nvmlDeviceGetHandleByIndex(self._dev)
+
+        def read():
+            return (pynvml.nvmlDeviceGetPcieThroughput(handle, pynvml.NVML_PCIE_UTIL_RX_BYTES),
+                    pynvml.nvmlDeviceGetPcieThroughput(handle, pynvml.NVML_PCIE_UTIL_TX_BYTES))
+        return read
+
+    def start(self) -> "PcieSampler":
+        if self._read is None:
+            self._read = self._nvml_reader()
+        self._stop.clear()
+        self.rx_bytes = self.tx_bytes = 0.0
+        self.samples = 0
+
+        def loop():
+            import time
+            last = time.perf_counter()
+            while not self._stop.wait(self.period_s):
+                now = time.perf_counter()
+                rx, tx = self._read()
+                self.rx_bytes += float(rx) * 1024.0 * (now - last)
+                self.tx_bytes += float(tx) * 1024.0 * (now - last)
+                self.samples += 1
+                last = now
+        self._thread = threading.Thread(target=loop, daemon=True)
+        self._thread.start()
+        return self
+
+    def stop(self) -> None:
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout=5)

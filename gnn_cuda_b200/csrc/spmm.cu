@@ -79,6 +79,10 @@ constexpr uint32_t kSegTag = 0x80000000u;
 #ifndef GNN_SPMM_U_NV34
 #define GNN_SPMM_U_NV34 2
 #endif
+#ifndef GNN_SPMM_PREFETCH_FIRST
+// per-row kernel: load the next row's first 32 columns while the current row is gathered
+#define GNN_SPMM_PREFETCH_FIRST 1
+#endif
 #ifndef GNN_SPMM_MIN_BLOCKS
 // at F <= 128 (one float4 per lane); wider rows keep 2. Measured on B200 with the
 // degree-ordered rows: 4 blocks (32 registers) 3.06 ms vs 3 blocks (40) 3.26 ms per
@@ -494,7 +498,7 @@ __global__ void __launch_bounds__(kBlockThreads, resident_blocks<NV>())
   };
   int c_next = 0;
   float w_next = 0.0f;
-  first_chunk(0, c_next, w_next);
+  if (GNN_SPMM_PREFETCH_FIRST) first_chunk(0, c_next, w_next);
   for (int i = 0; i < kRowsPerWarp; ++i) {
     const int64_t r = __shfl_sync(kFull, my_row, i);  // widened for the output offset
     if (r < 0) break;
@@ -503,13 +507,14 @@ __global__ void __launch_bounds__(kBlockThreads, resident_blocks<NV>())
     const float rs = __shfl_sync(kFull, my_rs, i);
     const int c_cur = c_next;
     const float w_cur = w_next;
-    if (i + 1 < kRowsPerWarp) first_chunk(i + 1, c_next, w_next);
+    if (GNN_SPMM_PREFETCH_FIRST && i + 1 < kRowsPerWarp) first_chunk(i + 1, c_next, w_next);
     const int64_t deg = static_cast<int64_t>(end - beg);
     if (deg > a.long_thr) continue;  // owned by a long-row CTA
     float4 acc[NV];
 #pragma unroll
     for (int q = 0; q < NV; ++q) acc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
-    accumulate_edges<WM, HOT, NV, U, IdxT>(a, beg, end, rs, lane, col0, valid, acc, true, c_cur, w_cur);
+    accumulate_edges<WM, HOT, NV, U, IdxT>(a, beg, end, rs, lane, col0, valid, acc, GNN_SPMM_PREFETCH_FIRST != 0,
+                                           c_cur, w_cur);
     float4* orow = reinterpret_cast<float4*>(a.out + r * a.ldo);
 #pragma unroll
     for (int q = 0; q < NV; ++q) {

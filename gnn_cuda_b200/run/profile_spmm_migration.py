@@ -119,8 +119,20 @@ def profile(a) -> dict:
     if a.synthetic:
         load = _synthetic_loader(a.synthetic, a.framework, a.device)
     window = {}
-    cap = {"on_measure_begin": lambda: window.__setitem__("t0", UMProfiler.timestamp()),
-           "on_measure_end": lambda: window.__setitem__("t1", UMProfiler.timestamp())}
+    pcie = None
+    if prof is None:
+        # no unified-memory counters: the host-link bytes of the measured loop from NVML instead
+        try:
+            from gnn_cuda_b200.GNN_cuda_common.um_profiler import PcieSampler
+            pcie = PcieSampler(torch.device(a.device).index or 0)
+            pcie._read = pcie._nvml_reader()
+        except Exception as e:  # no NVML either: SpMM time only
+            pcie = None
+            print(f"warning: no NVML PCIe counters either ({e})", file=sys.stderr)
+    cap = {"on_measure_begin": lambda: (window.__setitem__("t0", UMProfiler.timestamp()) if prof is not None
+                                        else pcie.start() if pcie is not None else None),
+           "on_measure_end": lambda: (window.__setitem__("t1", UMProfiler.timestamp()) if prof is not None
+                                      else pcie.stop() if pcie is not None else None)}
     out = io.StringIO()
     with contextlib.redirect_stdout(out):
         rc = run(framework_label=a.framework, select_device=npz_utils.select_device, load_graph_features=load,
@@ -140,6 +152,10 @@ def profile(a) -> dict:
             um = prof.totals((lo, hi), (window["t0"], window["t1"]))
             um = {k: (v / iters if isinstance(v, float) else v) for k, v in um.items()}
         prof.stop()
+    if pcie is not None and pcie.samples:
+        iters = max(1, int(cap["iters"]))
+        um = dict(um, htod_bytes=pcie.rx_bytes / iters, dtoh_bytes=pcie.tx_bytes / iters)
+        counters = "nvml-pcie: whole-device host-link bytes per iteration of the measured loop (no fault count)"
     return {"spmm_ns": float(cap["spmm_avg_ns"]), "htod_bytes": um["htod_bytes"], "dtoh_bytes": um["dtoh_bytes"],
             "gpu_faults": um["gpu_page_faults"], "records": um["records"], "dropped_records": um["dropped_records"],
             "counters": counters or "cupti", "stdout": out.getvalue()}
