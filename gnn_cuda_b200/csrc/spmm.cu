@@ -79,6 +79,10 @@ constexpr uint32_t kSegTag = 0x80000000u;
 #ifndef GNN_SPMM_U_NV34
 #define GNN_SPMM_U_NV34 2
 #endif
+#ifndef GNN_SPMM_LONG_SERIAL
+// 0: the long-row kernel runs on a side stream beside the per-row kernel; 1: before it, on the caller's stream
+#define GNN_SPMM_LONG_SERIAL 0
+#endif
 #ifndef GNN_SPMM_PREFETCH_FIRST
 // per-row kernel: load the next row's first 32 columns while the current row is gathered
 #define GNN_SPMM_PREFETCH_FIRST 1
@@ -1132,7 +1136,22 @@ int launch_vec(SpmmArgs a, cudaStream_t stream) {
     const int64_t gx = normal_blocks;
     if (gx > 0x7fffffffLL) return fail(GNN_ERR_UNSUPPORTED, "spmm: too many rows for one launch");
     SideStream* side = nullptr;
-    if (a.long_cap > 0) {
+    if (a.long_cap > 0 && GNN_SPMM_LONG_SERIAL) {
+      // long rows first, on the caller's stream (no fork / join)
+      const int long_blocks = static_cast<int>(
+          std::min<int64_t>(a.long_cap + a.seg_cap, static_cast<int64_t>(GNN_SPMM_LONG_CTAS_PER_SM) * sm_count()));
+      const size_t long_smem = static_cast<size_t>(a.long_split) * 32 * nv * sizeof(float4);
+      dim3 lgrid(static_cast<unsigned>(long_blocks), static_cast<unsigned>(tiles));
+#define GNN_LAUNCH_NV(NVV) spmm_long_kernel<WM, MEAN, HOT, NVV, IdxT><<<lgrid, block, long_smem, stream>>>(a)
+      switch (nv) {
+        case 1: GNN_LAUNCH_NV(1); break;
+        case 2: GNN_LAUNCH_NV(2); break;
+        case 3: GNN_LAUNCH_NV(3); break;
+        default: GNN_LAUNCH_NV(4); break;
+      }
+#undef GNN_LAUNCH_NV
+      GNN_LAUNCH_CHECK("spmm long-row kernel launch");
+    } else if (a.long_cap > 0) {
       int rc = side_stream(&side);
       if (rc != GNN_OK) return rc;
       side->mu.lock();
