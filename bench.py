@@ -66,6 +66,9 @@ def parse_args():
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU-baseline sample time (0: skip)")
     ap.add_argument("--scale", type=float, default=1.0, help="scale the graph down (smoke runs only)")
+    ap.add_argument("--gin-path", choices=["chunks", "fused"], default="chunks",
+                    help="gin_papers_like at full size: the separate calls over row ranges, or one fused kernel per "
+                         "layer (same bits)")
     ap.add_argument("--no-check", dest="check", action="store_false",
                     help="skip the check of sampled output rows against the oracle after the timed region")
     ap.add_argument("--no-reference-gpu", dest="reference_gpu", action="store_false",
@@ -937,6 +940,7 @@ def run_sage(args, device: torch.device) -> dict:
 # ---------------------------------------------------------------------------
 
 GIN_FEAT, GIN_LAYERS = 128, 3
+GIN_ROW_CHUNKS = 32
 
 
 def run_gin(args, device: torch.device) -> dict:
@@ -965,15 +969,20 @@ def run_gin(args, device: torch.device) -> dict:
     w1 = [synth.glorot(GIN_FEAT, GIN_FEAT, seed=args.seed + 10 + i, device=device) for i in range(GIN_LAYERS)]
     w2 = [synth.glorot(GIN_FEAT, GIN_FEAT, seed=args.seed + 20 + i, device=device) for i in range(GIN_LAYERS)]
     b = [torch.zeros(GIN_FEAT, device=device) for _ in range(GIN_LAYERS)]
-    fused = scale >= 0.5 and fused_ops.fused_supported(GIN_FEAT, GIN_FEAT, GIN_FEAT)
+    # full size: the separate calls over 32 row ranges (two [N/32, F] buffers), or one fused
+    # kernel per layer (--gin-path fused); both give the separate calls' bits
+    path = "whole" if scale < 0.5 else args.gin_path
+    if path == "fused" and not fused_ops.fused_supported(GIN_FEAT, GIN_FEAT, GIN_FEAT):
+        path = "chunks"
+    fused = path == "fused"
     torch.cuda.empty_cache()
     outs = [torch.empty(n, GIN_FEAT, device=device) for _ in range(2)]
-    if not fused:
+    if path == "whole":
         agg = torch.empty(n, GIN_FEAT, device=device)
         hid = torch.empty(n, GIN_FEAT, device=device)
     torch.cuda.synchronize(device)
     log(f"[bench] gin graph n={n} nnz={nnz} built in {time.time() - t0:.1f}s; "
-        f"{'fused layers' if fused else 'separate calls'}; "
+        f"{ {'fused': 'fused layers', 'chunks': f'separate calls over {GIN_ROW_CHUNKS} row ranges', 'whole': 'separate calls'}[path]}; "
         f"{torch.cuda.memory_allocated(device) / 1e9:.1f} GB allocated")
     timers: dict = {}
 
@@ -984,6 +993,10 @@ def run_gin(args, device: torch.device) -> dict:
             ev = partition._mark(tm, "spmm_begin")
             if fused:
                 fused_ops.gin_layer_forward_(rp, ci, h, 0.0, w1[li], b[li], w2[li], b[li], o, li != GIN_LAYERS - 1)
+                partition._mark(tm, "spmm_end", ev)
+            elif path == "chunks":
+                fused_ops.gin_layer_row_chunks_(rp, ci, h, 0.0, w1[li], b[li], w2[li], b[li], o, li != GIN_LAYERS - 1,
+                                                chunks=GIN_ROW_CHUNKS)
                 partition._mark(tm, "spmm_end", ev)
             else:
                 agg_ops.spmm_sum_forward_(rp, ci, h, agg)
@@ -1021,13 +1034,17 @@ def run_gin(args, device: torch.device) -> dict:
                 "nodes and entries, N(0,1) features, Glorot weights, zero bias",
         "config": {"workload": f"gin_papers_like x{scale:g}: GIN 3 layers, eps = 0, MLP Linear(128,128)-ReLU-"
                                "Linear(128,128), ReLU between layers", "nodes": n, "csr_entries": nnz,
-                   "layer": "fused aggregation + MLP (one kernel per layer)" if fused else "separate calls",
+                   "layer": {"fused": "fused aggregation + MLP (one kernel per layer)",
+                             "chunks": f"separate calls over {GIN_ROW_CHUNKS} row ranges (two [N/{GIN_ROW_CHUNKS}, F] "
+                                       "buffers)", "whole": "separate calls"}[path],
                    "feat_dim": GIN_FEAT, "layers": GIN_LAYERS, "self_loops": False,
                    "row_ptr": "int64" if rp.dtype == torch.int64 else "int32", "row_order": row_order(),
                    "l2": "inputs larger than L2 (X is %.1f GB), no flush" % (n * GIN_FEAT * 4 / 1e9)},
-        "roofline": {"bound": "hbm", "kernel": ("fused_layer_kernel + spmm_long_kernel (sum aggregation and MLP; "
-                                                "the time includes the two transforms)") if fused else
-                     "spmm_vec_kernel + spmm_long_kernel (sum aggregation)",
+        "roofline": {"bound": "hbm", "kernel": {"fused": "fused_layer_kernel + spmm_long_kernel (sum aggregation and "
+                                                         "MLP; the time includes the two transforms)",
+                                                "chunks": "spmm_vec_kernel + spmm_long_kernel + the MLP, per row range "
+                                                          "(the time includes the add and the two transforms)",
+                                                "whole": "spmm_vec_kernel + spmm_long_kernel (sum aggregation)"}[path],
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
                      "peak_source": peak_kind, "spmm_ms_per_layer": round(spmm_ms, 4),
                      "algorithmic_bytes_per_layer": bytes_layer, "traffic": None},

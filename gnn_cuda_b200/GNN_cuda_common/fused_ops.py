@@ -99,3 +99,49 @@ def mean_linear_forward_(row_ptr, col_ind, x, weight, bias, out, relu: bool = Fa
     _check_bias(bias, out)
     agg = N.GNN_AGG_MEAN_RECIPROCAL if reciprocal else N.GNN_AGG_MEAN
     _call(row_ptr, col_ind, None, agg, x, 1.0, False, weight, bias, relu, None, None, False, out)
+
+
+def gin_layer_row_chunks_(row_ptr, col_ind, x, eps: float, weight1, bias1, weight2, bias2, out,
+                          relu_out: bool = False, chunks: int = 16) -> None:
+    """The GIN layer of gin_layer_forward_ as the separate calls (spmm_sum_forward_,
+    tensor_add_inplace_, two linear_forward_) applied to `chunks` row ranges in turn,
+    so the aggregate and hidden matrices only ever hold one range's rows.
+
+    Same bits as the separate calls on the whole graph (and so as the fused
+    kernel): each range is aggregated with the whole graph's long-row threshold,
+    and every other step is row-wise. Faster than the fused kernel (the
+    aggregation keeps the per-row kernel's occupancy) at the cost of two
+    [N / chunks, F] buffers."""
+    from .native_ops import linear_forward_, tensor_add_inplace_
+    _check_inputs(row_ptr, col_ind, x, out, {"weight1": weight1, "weight2": weight2})
+    _check(x.size(0) == out.size(0), "x and out must have the same number of rows")
+    _check(x.size(1) == weight1.size(0) and weight1.size(1) == weight2.size(0) and out.size(1) == weight2.size(1),
+           "Inner GEMM dimensions must match")
+    n, f, nnz = out.size(0), x.size(1), col_ind.numel()
+    if n == 0:
+        return
+    lib = N.lib()
+    dev = out.device
+    rows = -(-n // max(1, int(chunks)))
+    agg = torch.empty(rows, f, device=dev)
+    hid = torch.empty(rows, weight1.size(1), device=dev)
+    alpha = float(torch.tensor(1.0 + float(eps), dtype=torch.float32))
+    old = N.config_get("spmm.long_row_threshold")
+    N.config_set("spmm.long_row_threshold", int(lib.gnn_spmm_long_row_threshold(n, nnz)))
+    starts = list(range(0, n, rows))
+    offs = row_ptr[torch.tensor(starts + [n], device=row_ptr.device)].to(torch.int64).cpu().tolist()
+    try:
+        with torch.cuda.device(dev):
+            for i, r0 in enumerate(starts):
+                m = min(n, r0 + rows) - r0
+                m_nnz = offs[i + 1] - offs[i]
+                ws, wsb = _workspace(dev, lib.gnn_spmm_schedule_workspace_bytes(m, m_nnz))
+                # rows [r0, r0 + m): row_ptr from entry r0 on (its offsets index col_ind as they are)
+                N.call("gnn_spmm_sum_forward", row_ptr.data_ptr() + r0 * row_ptr.element_size(),
+                       _index_type(row_ptr), col_ind.data_ptr() if nnz else None, x.data_ptr(), agg.data_ptr(), m,
+                       m_nnz, f, ws, wsb, _stream(dev))
+                tensor_add_inplace_(agg[:m], x[r0:r0 + m], alpha)
+                linear_forward_(agg[:m], weight1, bias1, hid[:m], True)
+                linear_forward_(hid[:m], weight2, bias2, out[r0:r0 + m], relu_out)
+    finally:
+        N.config_set("spmm.long_row_threshold", old)

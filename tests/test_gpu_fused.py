@@ -182,3 +182,29 @@ def test_refusals():
                                       ctypes.c_void_p(w.data_ptr()), None, 128, 0, None, None, 0, 0,
                                       ctypes.c_void_p(out.data_ptr()), None, 0, None)
     assert rc == 1 and "aggregation must be" in N.last_error()
+
+
+@pytest.mark.parametrize("chunks", [1, 3, 16])
+def test_gin_row_chunks_bit_exact_vs_separate_calls(chunks):
+    """The GIN layer run as the separate calls over row ranges (gin_layer_row_chunks_)
+    equals the whole-graph calls bit for bit, hub rows included."""
+    N.config_set("spmm.long_row_threshold", 0)
+    n, f = 12000, 128
+    rp, ci, _ = _hub_graph(n, seed=41, loops=False, index=torch.int64)
+    x = synth.features(n, f, seed=42, device=DEV)
+    w1 = synth.glorot(f, f, seed=43, device=DEV)
+    w2 = synth.glorot(f, f, seed=44, device=DEV)
+    b1 = torch.randn(f, generator=torch.Generator(device=DEV).manual_seed(45), device=DEV)
+    b2 = torch.randn(f, generator=torch.Generator(device=DEV).manual_seed(46), device=DEV)
+    agg = torch.empty(n, f, device=DEV)
+    hid = torch.empty(n, f, device=DEV)
+    ref = torch.empty(n, f, device=DEV)
+    agg_ops.spmm_sum_forward_(rp, ci, x, agg)
+    agg_ops.tensor_add_inplace_(agg, x, 1.0)
+    agg_ops.linear_forward_(agg, w1, b1, hid, True)
+    agg_ops.linear_forward_(hid, w2, b2, ref, True)
+    out = torch.full((n, f), float("nan"), device=DEV)
+    fused_ops.gin_layer_row_chunks_(rp, ci, x, 0.0, w1, b1, w2, b2, out, True, chunks=chunks)
+    torch.cuda.synchronize()
+    assert np.array_equal(_bits(out), _bits(ref))
+    assert N.config_get("spmm.long_row_threshold") == 0  # restored
