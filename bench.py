@@ -71,6 +71,8 @@ def parse_args():
                          "ranges (same bits; measured on one B200: 288 vs 370 ms per layer)")
     ap.add_argument("--no-check", dest="check", action="store_false",
                     help="skip the check of sampled output rows against the oracle after the timed region")
+    ap.add_argument("--no-other-configs", dest="other_configs", action="store_false",
+                    help="skip the Pubmed- and Reddit-shaped configurations measured after the headline")
     ap.add_argument("--no-reference-gpu", dest="reference_gpu", action="store_false",
                     help="skip timing the reference's own CUDA kernels on the same tensors")
     ap.add_argument("--chunks", type=int, default=0,
@@ -480,7 +482,31 @@ def run_ours(args, rank: int, world: int, device: torch.device):
         result["reference_gpu"] = reference_gpu_baseline(prob, device, args.seed, args.scale)
     if world == 1 and args.cpu_seconds > 0:
         result["cpu_baseline"] = cpu_baseline(prob, args.cpu_seconds)
+    if world == 1 and args.other_configs and args.scale == 1.0:
+        del prob, bufs
+        torch.cuda.empty_cache()
+        result["other_configs"] = other_configs(args, device)
     return result
+
+
+def other_configs(args, device) -> dict:
+    """The Pubmed-shaped one-layer GCN and the Reddit-shaped GraphSAGE forward, measured
+    in the same run (10 timed steps after 3 warm-up steps each), so that every
+    configuration that fits one GPU quickly has a number from the default bench."""
+    import copy
+    sub = copy.copy(args)
+    sub.steps, sub.warmup, sub.cpu_seconds, sub.e2e_steps = 10, 3, 0.0, 2
+    keep = ("metric", "value", "unit", "ms_per_step", "ms_per_layer", "roofline", "parity", "config", "e2e",
+            "gpu_launches")
+    out = {}
+    for name, fn in (("gcn_pubmed_like", run_pubmed), ("sage_reddit_like", run_sage)):
+        try:
+            r = fn(sub, device)
+            out[name] = {k: r[k] for k in keep if k in r}
+        except Exception as e:  # reported, never fatal for the headline line
+            out[name] = {"error": str(e)[:300]}
+        torch.cuda.empty_cache()
+    return out
 
 
 # ---------------------------------------------------------------------------
