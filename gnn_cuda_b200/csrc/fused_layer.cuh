@@ -16,9 +16,10 @@
 //   warps 0..15   gather: each takes 8 rows of the tile and sums their
 //                 neighbour rows exactly as spmm_vec_kernel does (one warp per
 //                 row, CSR order, 128-bit gathers), then stores the row into
-//                 the tile (and, for GIN, adds (1+eps)·x[row] first);
-//   warp 16       MMA issue (one thread) and TMEM allocation;
-//   warps 17..20  epilogue: TMEM -> registers, + bias, ReLU, out rows (GIN:
+//                 the tile (and, for GIN, adds (1+eps)·x[row] first); warp 0
+//                 also owns TMEM and, from lane 0, issues the tile's MMAs
+//                 (every gather warp waits for them before its next tile anyway);
+//   warps 16..19  epilogue: TMEM -> registers, + bias, ReLU, out rows (GIN:
 //                 the hidden layer goes back into the tile as the second MMA's
 //                 A operand, then the second epilogue writes out).
 //
