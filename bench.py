@@ -318,6 +318,17 @@ def run_ours(args, rank: int, world: int, device: torch.device):
         dist.barrier()
     launches = N.lib().gnn_kernel_launches() - launches0
     ms_total = t_start.elapsed_time(t_end)
+    trace = None
+    if world > 1 and args.exchange in ("push", "halo"):
+        # one more step with a timeline of its phases on every rank (not part of the timed steps)
+        ev_list: list = []
+        partition.gcn_forward_push(shard, prob["dis"], prob["x"], prob["ws"], prob["bs"], layout, exchange,
+                                   bufs["agg"], bufs["out"], halo=halo, trace=ev_list)
+        torch.cuda.synchronize(device)
+        trace = partition.trace_offsets(ev_list)
+        everyone: list = [None] * world
+        dist.all_gather_object(everyone, trace)
+        trace = everyone
     parity = None
     if world == 1 and args.check:
         # the last timed step left h1 in out0, the layer-2 aggregate in agg, the output in out1
@@ -464,7 +475,8 @@ def run_ours(args, rank: int, world: int, device: torch.device):
                                   "count too, so it can exceed 1); frac_dram = measured DRAM bytes / the same time / "
                                   "peak",
                      "spmm_ms_per_rank": [round(float(v), 4) for v in table[:, 2]],
-                     "exchange_wait_ms_per_step_per_rank": [round(float(v), 4) for v in table[:, 5]]},
+                     "exchange_wait_ms_per_step_per_rank": [round(float(v), 4) for v in table[:, 5]],
+                     "step_timeline_ms_per_rank": trace},
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h), "ms_per_step": round(e2e_ms / args.e2e_steps, 3),
                 "copies": ("overlapped across steps (two input sets and two output buffers; inputs up / output "

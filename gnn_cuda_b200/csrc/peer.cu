@@ -175,24 +175,29 @@ struct ListedTargets {
   int64_t off[kMaxPeers + 1];  // rows [off[q], off[q+1]) of the id list go to dst[q]
 };
 
-// One warp per listed row: copies row `ids[w]` (row_bytes, 16-byte words) from
-// src to the same row of the destination that owns list entry w. Every
+// One warp per listed row: copies row ids[e] (row_bytes, 16-byte words) from
+// src to the same row of the destination that owns list entry e. Every
 // destination shares src's row layout, so the row offset is the same on both
 // sides. Ids outside [0, max_rows) are skipped (the host validated them).
+// Work item w goes to destination w % ntargets, entry w / ntargets of that
+// destination's list: every destination is written at the same time. Walking
+// the lists destination after destination instead made every rank write to the
+// same peer at once (all ranks' lists share the peer order), so one GPU's
+// incoming links carried the traffic of seven senders while the others idled.
 __global__ void __launch_bounds__(512) push_listed_rows_kernel(const char* __restrict__ src, ListedTargets t,
                                                                int ntargets, const int32_t* __restrict__ ids,
-                                                               int64_t row_words, int64_t max_rows) {
+                                                               int64_t row_words, int64_t max_rows,
+                                                               int64_t max_count) {
   const int lane = threadIdx.x & 31;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
-  const int64_t total = t.off[ntargets];
-  for (int64_t w = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); w < total;
+  const int64_t items = max_count * ntargets;
+  for (int64_t w = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); w < items;
        w += warps) {
-    int q = 0;
-#pragma unroll
-    for (int p = 1; p < kMaxPeers; ++p) {
-      if (p < ntargets && w >= t.off[p]) q = p;
-    }
-    const int64_t row = ids[w];
+    const int q = static_cast<int>(w % ntargets);
+    const int64_t j = w / ntargets;
+    const int64_t e = t.off[q] + j;
+    if (e >= t.off[q + 1]) continue;  // this destination's list is shorter
+    const int64_t row = ids[e];
     if (row < 0 || row >= max_rows) continue;
     const int4* s = reinterpret_cast<const int4*>(src) + row * row_words;
     int4* d = reinterpret_cast<int4*>(t.dst[q]) + row * row_words;
@@ -235,10 +240,12 @@ extern "C" int gnn_peer_push_rows(const void* src, void* const* dsts, int ndst, 
                 "every destination must be a 16-byte aligned, non-NULL pointer");
     t.dst[p] = static_cast<char*>(dsts[p]);
   }
-  const int64_t want = (total + 15) / 16;  // 16 warps per 512-thread CTA
+  int64_t max_count = 0;
+  for (int p = 0; p < ndst; ++p) max_count = std::max<int64_t>(max_count, t.off[p + 1] - t.off[p]);
+  const int64_t want = (max_count * ndst + 15) / 16;  // 16 warps per 512-thread CTA
   const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, ctas > 0 ? ctas : 4 * sm_count())));
   push_listed_rows_kernel<<<grid, 512, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const char*>(src), t, ndst, row_ids, row_bytes / 16, max_rows);
+      static_cast<const char*>(src), t, ndst, row_ids, row_bytes / 16, max_rows, max_count);
   GNN_LAUNCH_CHECK("peer row-list push kernel launch");
   clear_error();
   return GNN_OK;

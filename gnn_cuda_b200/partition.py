@@ -558,7 +558,8 @@ class PeerRowExchange:
 
 def gcn_forward_push(shard: PaddedShard, dis_pad: torch.Tensor, x_pad: torch.Tensor, weights: list[torch.Tensor],
                      biases: list[torch.Tensor], layout: PaddedLayout, exchange: PeerRowExchange, agg: torch.Tensor,
-                     out: torch.Tensor, timers: dict | None = None, halo: HaloPlan | None = None) -> torch.Tensor:
+                     out: torch.Tensor, timers: dict | None = None, halo: HaloPlan | None = None,
+                     trace: list | None = None) -> torch.Tensor:
     """Multi-layer GCN over a padded-layout shard; layer outputs pushed to the peers piece by piece.
 
     exchange: a PeerRowExchange over layout.padded_rows rows. agg: [Mc, F]
@@ -566,11 +567,15 @@ def gcn_forward_push(shard: PaddedShard, dis_pad: torch.Tensor, x_pad: torch.Ten
     aggregation and X·W + b (+ReLU) land in this rank's rows of the exchange's
     current copy, which are then pushed to the peers while the next piece is
     computed. With a `halo` plan only the rows each peer reads are pushed.
-    Returns this rank's [rows, F] output rows (local order).
+    Returns this rank's [rows, F] output rows (local order). With `trace`, a list,
+    (label, event) pairs are appended for one step's timeline: the start, every
+    piece's aggregation and transform end (compute stream), its push end (push
+    stream) and the end of the wait for the exchange.
     """
     layers = len(weights)
     mc = layout.chunk_rows
     h = x_pad
+    _trace(trace, "start")
     for li in range(layers):
         last = li == layers - 1
         for c, piece in enumerate(shard.pieces):
@@ -580,11 +585,13 @@ def gcn_forward_push(shard: PaddedShard, dis_pad: torch.Tensor, x_pad: torch.Ten
             ev = _mark(timers, "spmm_begin")
             spmm_gcn_shard(piece, dis_pad, h, a)
             _mark(timers, "spmm_end", ev)
+            _trace(trace, f"l{li}p{c}_agg")
             if last:
                 dst = out[c * mc:c * mc + piece.num_rows]
             else:
                 dst = exchange.buffer()[piece.row_begin:piece.row_end]
             native_ops.linear_forward_(a, weights[li], biases[li], dst, not last)
+            _trace(trace, f"l{li}p{c}_gemm")
             if not last:
                 ready = torch.cuda.Event()
                 ready.record()
@@ -592,11 +599,29 @@ def gcn_forward_push(shard: PaddedShard, dis_pad: torch.Tensor, x_pad: torch.Ten
                     exchange.push(piece.row_begin, piece.row_end, ready)
                 else:
                     exchange.push_rows(halo.ids[c], halo.offsets[c], halo.peers, ready)
+                for s in exchange.streams.values():
+                    _trace(trace, f"l{li}p{c}_push", s)
         if not last:
             ev = _mark(timers, "xchg_begin")
             h = exchange.finish()
             _mark(timers, "xchg_end", ev, series="xchg")
+            _trace(trace, f"l{li}_exchanged")
     return out[:shard.num_rows]
+
+
+def _trace(trace: list | None, label: str, stream=None) -> None:
+    """Append (label, timing event recorded on `stream` or the current stream)."""
+    if trace is None:
+        return
+    ev = torch.cuda.Event(enable_timing=True)
+    ev.record(stream)
+    trace.append((label, ev))
+
+
+def trace_offsets(trace: list) -> dict:
+    """{label: ms after the first event} of a synchronised trace (the last event of a label wins)."""
+    t0 = trace[0][1]
+    return {label: round(t0.elapsed_time(ev), 4) for label, ev in trace}
 
 
 def _mark(timers: dict | None, key: str, begin=None, *, series: str = "spmm"):
