@@ -82,9 +82,12 @@ def parse_args():
                          "the rows each peer reads (halo), or NCCL all_gather")
     ap.add_argument("--transport", choices=["sm", "ce"], default="sm",
                     help="push transport: one SM kernel storing to every peer, or copy engines")
-    ap.add_argument("--push-ctas", type=int, default=0, help="grid of the SM push kernel (0: 4 per SM)")
+    ap.add_argument("--push-ctas", type=int, default=0, help="grid of the halo push kernel (0: the library default, 1 per SM)")
     ap.add_argument("--layout", choices=["balanced", "contiguous"], default="balanced",
                     help="N > 1: rows dealt to ranks by cost, or contiguous cost-balanced ranges")
+    ap.add_argument("--padded-order", choices=["rank", "chunk"], default="rank",
+                    help="N > 1 with pushes: every rank's rows one block of the exchange matrix (the last layer "
+                         "then runs as one call), or piece-major blocks (the all_gather exchange always uses these)")
     ap.add_argument("--workload", choices=["gcn_products_like", "gcn_pubmed_like", "sage_reddit_like",
                                            "gin_papers_like", "locality_products_like"],
                     default="gcn_products_like",
@@ -217,8 +220,15 @@ def row_order() -> str:
                f"{N.config_get('spmm.schedule_window')} rows"}[mode]
 
 
+def default_chunks(chunks: int, world: int) -> int:
+    """Row pieces per rank: as given, else 2 from 8 GPUs up (on 8 B200s two pieces hide
+    most of the halo exchange behind the second piece's aggregation) and 1 below."""
+    return chunks if chunks > 0 else (2 if world >= 8 else 1)
+
+
 def describe(prob, world: int, gemm: str | None = None, chunks: int = 1, exchange: str = "halo",
-             transport: str = "sm", layout: str = "balanced", order: str | None = None) -> dict:
+             transport: str = "sm", layout: str = "balanced", order: str | None = None,
+             padded_order: str = "rank") -> dict:
     if gemm is None:
         gemm = "tcgen05-tf32" if N.lib().gnn_gemm_uses_tensor_cores(prob["n"], FEAT, FEAT) else "ffma-fp32"
     if order is None:
@@ -227,8 +237,10 @@ def describe(prob, world: int, gemm: str | None = None, chunks: int = 1, exchang
             "nodes": prob["n"], "csr_entries": int(prob["nnz"]), "feat_dim": FEAT, "layers": LAYERS,
             "self_loops": True, "graph": "R-MAT(0.57,0.19,0.19,0.05), symmetrised, de-duplicated",
             "parallelism": f"rows{world}" + ("" if world == 1 else
-                                             f"+{layout}_{transport}_push_pieces{chunks}" if exchange == "push" else
-                                             f"+{layout}_halo_push_pieces{chunks}" if exchange == "halo" else
+                                             f"+{layout}_{transport}_push_pieces{chunks}_{padded_order}_major"
+                                             if exchange == "push" else
+                                             f"+{layout}_halo_push_pieces{chunks}_{padded_order}_major"
+                                             if exchange == "halo" else
                                              f"+{layout}_nccl_allgather_pieces{chunks}"),
             "l2": "inputs larger than L2 (X is %.2f GB), no flush" % (prob["n"] * FEAT * 4 / 1e9),
             "gemm": gemm, "row_order": order}
@@ -245,9 +257,7 @@ def run_ours(args, rank: int, world: int, device: torch.device):
     rp_cpu = prob["rp"].to(torch.int64).cpu().numpy()
     exchange = None
     halo = None
-    if args.chunks <= 0:
-        # measured on B200: two pieces hide part of the exchange at 8 GPUs (3.42 vs 3.69 ms per step)
-        args.chunks = 2 if world >= 8 else 1
+    args.chunks = default_chunks(args.chunks, world)
     if world == 1:
         shard = partition.make_shard(prob["rp"], prob["ci"], 0, n)
         bufs = {"agg": torch.empty(n, FEAT, device=device), "out0": torch.empty(n, FEAT, device=device),
@@ -255,11 +265,17 @@ def run_ours(args, rank: int, world: int, device: torch.device):
     else:
         # rows dealt to ranks by cost (or contiguous ranges), renumbered into the padded
         # chunk-major exchange layout; sums are unchanged, only column ids are rewritten
+        rank_major = args.exchange in ("push", "halo") and args.padded_order == "rank"
         layout = partition.make_padded_layout(rp_cpu, world, args.chunks, balanced=args.layout == "balanced",
-                                              row_cost=partition.ROW_COST_IN_ENTRIES)
+                                              row_cost=partition.ROW_COST_IN_ENTRIES, rank_major=rank_major)
         shard = partition.make_padded_shard(prob["rp"], prob["ci"], layout, rank)
         if args.exchange == "halo":
             halo = partition.make_halo_plan(prob["rp"], prob["ci"], layout, rank)
+        # every rank sums its rows with the whole graph's long-row threshold, as one GPU
+        # does, so the partitioned forward gives the one-GPU forward's bits
+        N.config_set("spmm.long_row_threshold", int(N.lib().gnn_spmm_long_row_threshold(n, nnz)))
+        if args.check:
+            whole_graph = {k: prob[k] for k in ("rp", "ci", "dis", "x")}
         prob["dis"] = layout.pad_rows(prob["dis"])
         prob["x"] = layout.pad_rows(prob["x"])
         del prob["rp"], prob["ci"]
@@ -268,7 +284,8 @@ def run_ours(args, rank: int, world: int, device: torch.device):
             exchange = partition.PeerRowExchange(layout.padded_rows, FEAT, rank, world, device,
                                                  transport="sm" if args.exchange == "halo" else args.transport,
                                                  ctas=args.push_ctas)
-            bufs = {"agg": torch.empty(layout.chunk_rows, FEAT, device=device),
+            # with rank-major rows the last layer aggregates all of them in one call
+            bufs = {"agg": torch.empty(layout.local_rows if rank_major else layout.chunk_rows, FEAT, device=device),
                     "out": torch.empty(layout.local_rows, FEAT, device=device)}
         else:
             bufs = partition.allgather_buffers(layout, FEAT, device)
@@ -333,8 +350,13 @@ def run_ours(args, rank: int, world: int, device: torch.device):
     if world == 1 and args.check:
         # the last timed step left h1 in out0, the layer-2 aggregate in agg, the output in out1
         parity = check_forward_sample(prob, bufs["out0"], bufs["agg"], bufs["out1"], device)
+    elif args.check:
+        parity = check_partitioned_forward(whole_graph, prob["ws"], prob["bs"], layout, rank, step(), device)
+        del whole_graph
+        torch.cuda.empty_cache()
     # SpMM time per layer on this rank (summed over its row pieces when N > 1)
     spmm_ms = [b.elapsed_time(e) for b, e in timers.get("spmm", [])]
+    agg_calls = len(spmm_ms) // max(1, args.steps)
     spmm_ms_avg = sum(spmm_ms) / max(1, args.steps * LAYERS)
     # exposed exchange: how long the compute stream waits at each layer boundary
     xchg_ms = sum(b.elapsed_time(e) for b, e in timers.get("xchg", [])) / max(1, args.steps)
@@ -352,7 +374,7 @@ def run_ours(args, rank: int, world: int, device: torch.device):
     if world == 1:
         dev_in = [prob["rp"], prob["ci"], prob["dis"], prob["x"]]
     else:
-        dev_in = [t for p in shard.pieces for t in (p.row_ptr, p.col_ind) if t.numel()] + [prob["dis"], prob["x"]]
+        dev_in = shard.device_tensors() + [prob["dis"], prob["x"]]
     dev_in += prob["ws"] + prob["bs"]
     host_in = [t.cpu().pin_memory() for t in dev_in]
     in_sets = [dev_in]
@@ -460,12 +482,12 @@ def run_ours(args, rank: int, world: int, device: torch.device):
         "data": f"synthetic: seeded R-MAT graph (seed {args.seed}) with ogbn-products shape, N(0,1) features, "
                 "Glorot weights, zero bias",
         "config": describe(prob, world, chunks=args.chunks, exchange=args.exchange, transport=args.transport,
-                           layout=args.layout),
+                           layout=args.layout, padded_order=args.padded_order),
         "roofline": {"bound": "hbm", "kernel": "spmm_vec_kernel + spmm_long_kernel (GCN aggregation)",
                      "achieved": round(achieved, 1) if achieved else None, "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4) if achieved else None, "peak_source": peak_kind,
                      "spmm_ms_per_layer": round(spmm_ms_avg, 4), "algorithmic_bytes_per_layer": shard_bytes,
-                     "launches_per_layer": 1 if world == 1 else args.chunks,
+                     "aggregation_calls_per_step": agg_calls,
                      "traffic": traffic, "rank": slow,
                      "frac_dram": round(traffic / (spmm_ms_avg * 1e-3) / 1e9 / peak, 4) if traffic and spmm_ms_avg else None,
                      "l2_hit_rate": prof["l2_hit_rate"] if prof else None,
@@ -585,6 +607,30 @@ def check_forward_sample(prob, h1: torch.Tensor, agg2: torch.Tensor, out: torch.
             "ok": bool(same.all() and err_agg <= 1.0 and max(err_h1, err_out) <= 2e-3),
             "checked": "layer-1 output (TF32) and layer-2 aggregation (bits) and output (TF32) of the last timed "
                        "step, sampled rows (every long row + random others), against the C oracle"}
+
+
+def check_partitioned_forward(graph: dict, ws, bs, layout, rank: int, rows_out: torch.Tensor, device) -> dict:
+    """This rank's output rows of the partitioned forward against the same rows
+    of the one-GPU forward (the reference-facing calls over the whole graph, on
+    this rank's GPU), bit for bit; the count of differing rows is summed over
+    ranks. The one-GPU forward is itself checked against the oracle by the N = 1
+    line."""
+    agg = torch.empty(graph["x"].shape, device=device)
+    h = graph["x"]
+    for li in range(LAYERS):
+        gcn_ops.spmm_gcn_forward_(graph["rp"], graph["ci"], graph["dis"], h, agg)
+        o = torch.empty(h.shape[0], FEAT, device=device)
+        agg_ops.linear_forward_(agg, ws[li], bs[li], o, li != LAYERS - 1)
+        h = o
+    mine = h[layout.order[rank].to(device)]
+    differ = (mine.view(torch.int32) != rows_out.view(torch.int32)).any(dim=1).sum().to(torch.int64)
+    counts = torch.stack([differ, torch.tensor(rows_out.shape[0], dtype=torch.int64, device=device)])
+    dist.all_reduce(counts)
+    differ, total = (int(v) for v in counts.cpu())
+    return {"rows_checked": total, "rows_differing": differ, "ok": differ == 0,
+            "long_row_threshold": int(N.config_get("spmm.long_row_threshold")),
+            "checked": "every output row of the partitioned forward (one extra step after the timed region) "
+                       "against the one-GPU forward of the whole graph, bit for bit"}
 
 
 # ---------------------------------------------------------------------------
@@ -740,7 +786,9 @@ def run_reference(args):
     from oracle import oracle as O
     prob = build_problem(args.seed, torch.device("cpu"), args.scale)
     hp = _host_problem(prob)
-    cfg = describe(prob, args.gpus, gemm="cpu-fp32", order="CSR row order (C restatement, OpenMP over rows)")
+    cfg = describe(prob, args.gpus, gemm="cpu-fp32", order="CSR row order (C restatement, OpenMP over rows)",
+                   chunks=default_chunks(args.chunks, args.gpus), exchange=args.exchange, transport=args.transport,
+                   layout=args.layout, padded_order=args.padded_order)
     del prob
     threads = O.max_threads()
     total = args.steps + args.warmup

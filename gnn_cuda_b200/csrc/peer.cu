@@ -242,8 +242,11 @@ extern "C" int gnn_peer_push_rows(const void* src, void* const* dsts, int ndst, 
   }
   int64_t max_count = 0;
   for (int p = 0; p < ndst; ++p) max_count = std::max<int64_t>(max_count, t.off[p + 1] - t.off[p]);
+  // Default grid: one CTA per SM. Measured on 8 B200s (products-shaped graph, halo push beside
+  // the next piece's aggregation): 2.17 ms per step against 3.18 ms with four CTAs per SM,
+  // whose push CTAs held every SM while the peers waited at the layer boundary.
   const int64_t want = (max_count * ndst + 15) / 16;  // 16 warps per 512-thread CTA
-  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, ctas > 0 ? ctas : 4 * sm_count())));
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, ctas > 0 ? ctas : sm_count())));
   push_listed_rows_kernel<<<grid, 512, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const char*>(src), t, ndst, row_ids, row_bytes / 16, max_rows, max_count);
   GNN_LAUNCH_CHECK("peer row-list push kernel launch");

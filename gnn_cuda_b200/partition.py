@@ -146,10 +146,17 @@ class PaddedLayout:
     values; CSR entry order, and therefore every floating-point sum, is
     unchanged. With one rank's rows a contiguous range and chunks == 1 this is
     the plain layout r*Mc + i.
+
+    rank_major=True places local row i of rank r at r * chunks * Mc + i
+    instead: every rank's rows form one contiguous block (a layer can then run
+    as one call over all of them) and piece c is [Mc] rows inside it. The
+    peer-to-peer exchanges (push, halo) work with either; the all_gather
+    exchange needs the chunk-major order.
     """
     order: list[torch.Tensor]
     chunk_rows: int
     chunks: int = 1
+    rank_major: bool = False
 
     def __post_init__(self):
         self.order = [torch.as_tensor(o, dtype=torch.int64).cpu().contiguous() for o in self.order]
@@ -158,7 +165,10 @@ class PaddedLayout:
         mc, w = self.chunk_rows, self.world
         for r, o in enumerate(self.order):
             i = torch.arange(o.numel(), dtype=torch.int64)
-            ids[o] = (i // mc) * (w * mc) + r * mc + (i % mc)
+            if self.rank_major:
+                ids[o] = r * self.chunks * mc + i
+            else:
+                ids[o] = (i // mc) * (w * mc) + r * mc + (i % mc)
         if n and int(ids.min()) < 0:
             raise ValueError("the rank orders must cover every row exactly once")
         self.ids = ids
@@ -191,7 +201,19 @@ class PaddedLayout:
 
     def piece_first(self, rank: int, c: int) -> int:
         """Padded id of piece c's first row on `rank`."""
+        if self.rank_major:
+            return (rank * self.chunks + c) * self.chunk_rows
         return c * self.world * self.chunk_rows + rank * self.chunk_rows
+
+    def piece_of(self, padded: torch.Tensor) -> torch.Tensor:
+        """Piece index of each padded row id."""
+        if self.rank_major:
+            return (padded % (self.chunks * self.chunk_rows)) // self.chunk_rows
+        return padded // (self.world * self.chunk_rows)
+
+    def contiguous_ranks(self) -> bool:
+        """Every rank's rows are one contiguous block of padded ids."""
+        return self.rank_major or self.chunks == 1
 
     def ids_on(self, device) -> torch.Tensor:
         key = str(device)
@@ -231,9 +253,10 @@ def balanced_row_order(row_ptr: np.ndarray, world: int, row_cost: float = ROW_CO
 
 
 def make_padded_layout(row_ptr: np.ndarray, world: int, chunks: int = 1, *, balanced: bool = False,
-                       row_cost: float = 0.0) -> PaddedLayout:
+                       row_cost: float = 0.0, rank_major: bool = False) -> PaddedLayout:
     """Contiguous cost-balanced row ranges (balanced=False), or rows dealt by
-    balanced_row_order (balanced=True), in `chunks` pieces per rank."""
+    balanced_row_order (balanced=True), in `chunks` pieces per rank, placed
+    chunk-major or rank-major (PaddedLayout)."""
     if balanced:
         order = balanced_row_order(row_ptr, world, row_cost)
     else:
@@ -241,7 +264,7 @@ def make_padded_layout(row_ptr: np.ndarray, world: int, chunks: int = 1, *, bala
         order = [np.arange(bounds[r], bounds[r + 1]) for r in range(world)]
     max_rows = max(1, max(len(o) for o in order))
     chunks = max(1, min(int(chunks), max_rows))
-    return PaddedLayout(order, -(-max_rows // chunks), chunks)
+    return PaddedLayout(order, -(-max_rows // chunks), chunks, rank_major)
 
 
 @dataclass
@@ -249,6 +272,7 @@ class PaddedShard:
     """One rank's rows as `chunks` row pieces with padded row and column ids."""
     rank: int
     pieces: list[RowShard]  # piece c: row_begin = its first padded row (also the dis lookup)
+    whole: RowShard | None = None  # all rows as one shard, when they are contiguous padded ids
 
     @property
     def num_rows(self) -> int:
@@ -257,6 +281,14 @@ class PaddedShard:
     @property
     def num_edges(self) -> int:
         return sum(p.num_edges for p in self.pieces)
+
+    def device_tensors(self) -> list[torch.Tensor]:
+        """The distinct device tensors holding this shard (the pieces' column ids
+        are views of the whole shard's when it exists)."""
+        ts = [p.row_ptr for p in self.pieces if p.num_rows]
+        if self.whole is not None:
+            return ts + [self.whole.row_ptr, self.whole.col_ind]
+        return ts + [p.col_ind for p in self.pieces if p.num_edges]
 
 
 def make_padded_shard(row_ptr: torch.Tensor, col_ind: torch.Tensor, layout: PaddedLayout, rank: int) -> PaddedShard:
@@ -278,15 +310,19 @@ def make_padded_shard(row_ptr: torch.Tensor, col_ind: torch.Tensor, layout: Padd
     else:
         entry = starts.repeat_interleave(deg) + (torch.arange(total, device=dev) - local_rp[:-1].repeat_interleave(deg))
         cols_g = col_ind[entry]
-    cols = layout.padded_ids(cols_g).to(torch.int32) if total else col_ind[:0]
+    cols = layout.padded_ids(cols_g).to(torch.int32) if total else col_ind[:0].to(torch.int32)
     pieces = []
     for c in range(layout.chunks):
         lo, hi = layout.piece_range(rank, c)
         e0, e1 = int(local_rp[lo]), int(local_rp[hi])
         rp_c = (local_rp[lo:hi + 1] - e0).to(row_ptr.dtype).contiguous()
         head = layout.piece_first(rank, c)
-        pieces.append(RowShard(head, head + (hi - lo), rp_c, cols[e0:e1].contiguous()))
-    return PaddedShard(rank, pieces)
+        pieces.append(RowShard(head, head + (hi - lo), rp_c, cols[e0:e1]))  # a view of cols
+    whole = None
+    if layout.contiguous_ranks():
+        head = layout.piece_first(rank, 0)
+        whole = RowShard(head, head + int(rows.numel()), local_rp.to(row_ptr.dtype).contiguous(), cols)
+    return PaddedShard(rank, pieces, whole)
 
 
 @dataclass
@@ -315,7 +351,7 @@ def make_halo_plan(row_ptr: torch.Tensor, col_ind: torch.Tensor, layout: PaddedL
     (peer, column) pair where a row owned by the peer reads a column owned by
     `rank`, de-duplicated, as padded ids split by `rank`'s row pieces."""
     dev = row_ptr.device
-    n, w, mc = layout.num_nodes, layout.world, layout.chunk_rows
+    n, w = layout.num_nodes, layout.world
     owner = torch.empty(n, dtype=torch.int64, device=dev)
     for r, o in enumerate(layout.order):
         owner[o.to(dev)] = r
@@ -329,7 +365,7 @@ def make_halo_plan(row_ptr: torch.Tensor, col_ind: torch.Tensor, layout: PaddedL
     del owner, row_owner, col, sel, pid
     peer_of = key // total_rows
     ids = key - peer_of * total_rows
-    piece = ids // (w * mc)
+    piece = layout.piece_of(ids)
     peers = [p for p in range(w) if p != rank]
     out_ids, out_off = [], []
     for c in range(layout.chunks):
@@ -362,6 +398,8 @@ def gcn_forward_allgather(shard: PaddedShard, dis_pad: torch.Tensor, x_pad: torc
     compute stream goes on with piece c+1. The next layer waits for all
     pieces. Returns this rank's [rows, F] output rows (local order).
     """
+    if layout.rank_major and layout.chunks > 1:
+        raise ValueError("the all_gather exchange needs the chunk-major layout")
     x = x_pad
     layers = len(weights)
     mc, world = layout.chunk_rows, layout.world
@@ -563,10 +601,14 @@ def gcn_forward_push(shard: PaddedShard, dis_pad: torch.Tensor, x_pad: torch.Ten
     """Multi-layer GCN over a padded-layout shard; layer outputs pushed to the peers piece by piece.
 
     exchange: a PeerRowExchange over layout.padded_rows rows. agg: [Mc, F]
-    scratch. out: [chunks*Mc, F] for the last layer (local order). Each piece's
-    aggregation and X·W + b (+ReLU) land in this rank's rows of the exchange's
-    current copy, which are then pushed to the peers while the next piece is
-    computed. With a `halo` plan only the rows each peer reads are pushed.
+    scratch, or [chunks*Mc, F]. out: [chunks*Mc, F] for the last layer (local
+    order). Each piece's aggregation and X·W + b (+ReLU) land in this rank's
+    rows of the exchange's current copy, which are then pushed to the peers
+    while the next piece is computed. With a `halo` plan only the rows each peer
+    reads are pushed. The last layer pushes nothing, so when the shard's rows
+    are one contiguous block (shard.whole) and agg holds them all it runs as
+    one aggregation call and one transform: the same per-row sums as the
+    pieces, without a call per piece.
     Returns this rank's [rows, F] output rows (local order). With `trace`, a list,
     (label, event) pairs are appended for one step's timeline: the start, every
     piece's aggregation and transform end (compute stream), its push end (push
@@ -576,9 +618,11 @@ def gcn_forward_push(shard: PaddedShard, dis_pad: torch.Tensor, x_pad: torch.Ten
     mc = layout.chunk_rows
     h = x_pad
     _trace(trace, "start")
+    whole_last = shard.whole is not None and shard.whole.num_rows <= agg.size(0) and len(shard.pieces) > 1
     for li in range(layers):
         last = li == layers - 1
-        for c, piece in enumerate(shard.pieces):
+        pieces = [shard.whole] if last and whole_last else shard.pieces
+        for c, piece in enumerate(pieces):
             if piece.num_rows == 0:
                 continue
             a = agg[:piece.num_rows]

@@ -483,8 +483,11 @@ int gnn_peer_push(const void* src, void* const* dsts, int ndst, size_t bytes, in
  * row_ids[row_offsets[q] .. row_offsets[q+1]) (row_offsets is a HOST array of
  * ndst + 1 entries starting at 0; row_ids is device int32) are copied from src
  * to the same row of dsts[q] (every buffer has the same [max_rows, row_bytes]
- * layout). One warp per listed row; ids outside [0, max_rows) are skipped.
- * row_bytes, src and every destination must be 16-byte aligned; ndst <= 8. */
+ * layout). One warp per listed row, the destinations' rows interleaved so that
+ * every peer receives at once; ids outside [0, max_rows) are skipped. ctas
+ * limits the grid (0 = 1 per SM, which leaves the other SMs' slots to the
+ * aggregation running beside the push). row_bytes, src and every destination
+ * must be 16-byte aligned; ndst <= 8. */
 int gnn_peer_push_rows(const void* src, void* const* dsts, int ndst, const int32_t* row_ids,
                        const int64_t* row_offsets, int64_t row_bytes, int64_t max_rows, int ctas,
                        gnn_stream_t stream);

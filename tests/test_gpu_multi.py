@@ -5,7 +5,9 @@ chunk-major layout; pushes into the peers' IPC-mapped buffers by the SM push
 kernel and by copy engines, and halo pushes of only the rows each peer reads
 (three steps in a row, so both alternating buffers are used, and the rows a
 halo push skips hold stale values that must never be read) — on contiguous
-row ranges and on rows dealt to ranks by cost, with 1 to 3 pieces per rank.
+row ranges and on rows dealt to ranks by cost, with 1 to 3 pieces per rank, in
+the chunk-major and the rank-major padded layouts (the latter with the last
+layer as one call over all of a rank's rows).
 
 Runs on 2 and on 4 GPUs where that many are visible (spawned ranks, one GPU each,
 NCCL with NVLS off). The long-row threshold is fixed so every rank uses the
@@ -66,11 +68,15 @@ def _worker(rank, world, port, q):
         # padded chunk-major layouts (contiguous ranges or rows dealt by cost), both exchanges
         padded = []
         rp_np = rp.cpu().numpy()
-        cases = [("allgather", None, 1, False), ("allgather", None, 3, True),
-                 ("push", "sm", 1, True), ("push", "ce", 3, True), ("push", "sm", 2, False),
-                 ("halo", "sm", 1, True), ("halo", "sm", 2, True), ("halo", "sm", 3, False)]
-        for how, transport, chunks, balanced in cases:
-            lay = partition.make_padded_layout(rp_np, world, chunks, balanced=balanced, row_cost=6)
+        # (exchange, transport, pieces, rows dealt by cost, rank-major layout); rank-major
+        # layouts run the last layer as one call over all of a rank's rows
+        cases = [("allgather", None, 1, False, False), ("allgather", None, 3, True, False),
+                 ("push", "sm", 1, True, False), ("push", "ce", 3, True, False), ("push", "sm", 2, False, False),
+                 ("halo", "sm", 1, True, False), ("halo", "sm", 2, True, False), ("halo", "sm", 3, False, False),
+                 ("halo", "sm", 2, True, True), ("push", "sm", 3, False, True)]
+        for how, transport, chunks, balanced, rank_major in cases:
+            lay = partition.make_padded_layout(rp_np, world, chunks, balanced=balanced, row_cost=6,
+                                               rank_major=rank_major)
             pshard = partition.make_padded_shard(rp, ci, lay, rank)
             dis_p, x_p = lay.pad_rows(dis), lay.pad_rows(x)
             if how == "allgather":
@@ -79,7 +85,7 @@ def _worker(rank, world, port, q):
             else:
                 ex = partition.PeerRowExchange(lay.padded_rows, FEAT, rank, world, dev, transport=transport)
                 halo = partition.make_halo_plan(rp, ci, lay, rank) if how == "halo" else None
-                agg = torch.empty(lay.chunk_rows, FEAT, device=dev)
+                agg = torch.empty(lay.local_rows if rank_major else lay.chunk_rows, FEAT, device=dev)
                 mine = torch.empty(lay.local_rows, FEAT, device=dev)
                 for _ in range(3):  # repeated steps alternate the two copies
                     pout = partition.gcn_forward_push(pshard, dis_p, x_p, ws, bs, lay, ex, agg, mine, halo=halo)
@@ -88,8 +94,12 @@ def _worker(rank, world, port, q):
             pfull[:pshard.num_rows] = pout
             gathered = torch.empty(lay.padded_rows, FEAT, device=dev)
             mc = lay.chunk_rows
-            for c in range(lay.chunks):
-                dist.all_gather_into_tensor(gathered[c * world * mc:(c + 1) * world * mc], pfull[c * mc:(c + 1) * mc])
+            if rank_major:
+                dist.all_gather_into_tensor(gathered, pfull)
+            else:
+                for c in range(lay.chunks):
+                    dist.all_gather_into_tensor(gathered[c * world * mc:(c + 1) * world * mc],
+                                                pfull[c * mc:(c + 1) * mc])
             padded.append(lay.unpad_rows(gathered).cpu().numpy())
             if how in ("push", "halo"):
                 ex.close()

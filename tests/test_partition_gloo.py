@@ -125,14 +125,16 @@ def test_balanced_row_order(world):
     assert all(np.all(np.diff(o) > 0) for o in order)  # increasing ids within a rank
 
 
+@pytest.mark.parametrize("rank_major", [False, True])
 @pytest.mark.parametrize("world,chunks,balanced", [(2, 3, False), (3, 2, False), (4, 5, True), (2, 64, True),
                                                    (3, 1, True)])
-def test_padded_layout_chunk_major(world, chunks, balanced):
+def test_padded_layout_pieces(world, chunks, balanced, rank_major):
     u, v = synth.rmat_undirected(300, 2000, seed=world + chunks)
     s, d = synth.symmetrize(u, v)
     from gnn_cuda_b200.GNN_cuda_common import graph_utils as G
     g = G.build_gcn_normalized_csr(s, d, num_nodes=300)
-    lay = partition.make_padded_layout(g.row_ptr.numpy(), world, chunks, balanced=balanced, row_cost=6)
+    lay = partition.make_padded_layout(g.row_ptr.numpy(), world, chunks, balanced=balanced, row_cost=6,
+                                       rank_major=rank_major)
     ids = lay.padded_ids(torch.arange(300))
     assert len(set(ids.tolist())) == 300 and int(ids.max()) < lay.padded_rows  # injective, in range
     mc = lay.chunk_rows
@@ -143,6 +145,9 @@ def test_padded_layout_chunk_major(world, chunks, balanced):
             got = ids[rows[lo:hi]]
             want = lay.piece_first(r, c) + torch.arange(hi - lo)
             assert torch.equal(got, want)  # piece c of rank r is one contiguous block
+            assert bool((lay.piece_of(got) == c).all())
+        if lay.contiguous_ranks():  # all of rank r's rows are one block
+            assert torch.equal(ids[rows], lay.piece_first(r, 0) + torch.arange(rows.numel()))
     # the shard holds exactly its rows' entries, in CSR order, renumbered
     rp = g.row_ptr.to(torch.int64)
     for r in range(world):
@@ -158,6 +163,11 @@ def test_padded_layout_chunk_major(world, chunks, balanced):
             seg = rows[lo:hi]
             assert int(p.row_ptr[0]) == 0
             assert torch.equal(torch.diff(p.row_ptr.to(torch.int64)), rp[seg + 1] - rp[seg])  # row degrees
+        assert (sh.whole is not None) == lay.contiguous_ranks()
+        if sh.whole is not None:  # the whole shard is the pieces laid end to end
+            assert sh.whole.row_begin == lay.piece_first(r, 0) and sh.whole.num_rows == rows.numel()
+            assert torch.equal(sh.whole.col_ind.to(torch.int64), cols)
+            assert torch.equal(torch.diff(sh.whole.row_ptr.to(torch.int64)), rp[rows + 1] - rp[rows])
     x = torch.randn(300, 3)
     assert torch.equal(lay.unpad_rows(lay.pad_rows(x)), x)
 
@@ -249,8 +259,10 @@ def test_two_rank_exchange_matches_single_rank():
         assert np.array_equal(results[r].view(np.uint32), ref.view(np.uint32))
 
 
-@pytest.mark.parametrize("world,chunks,balanced", [(2, 1, True), (3, 2, True), (4, 3, False), (8, 2, True)])
-def test_halo_plan_delivers_every_row_a_rank_reads(world, chunks, balanced):
+@pytest.mark.parametrize("world,chunks,balanced,rank_major", [(2, 1, True, False), (3, 2, True, False),
+                                                              (4, 3, False, False), (8, 2, True, False),
+                                                              (3, 2, True, True), (8, 2, True, True)])
+def test_halo_plan_delivers_every_row_a_rank_reads(world, chunks, balanced, rank_major):
     """Emulates the halo exchange on the CPU: every rank writes its own rows into
     its copy of the next layer's input (the rest NaN), then each rank's listed
     rows are copied into the listed peers' copies. Every row a rank's CSR reads
@@ -259,7 +271,8 @@ def test_halo_plan_delivers_every_row_a_rank_reads(world, chunks, balanced):
     u, v = synth.rmat_undirected(n, n * 6, seed=71)
     s, d = synth.symmetrize(u, v)
     rp, ci, _ = synth.csr_on_device(s, d, n, add_self_loops=True)
-    lay = partition.make_padded_layout(rp.numpy(), world, chunks, balanced=balanced, row_cost=6)
+    lay = partition.make_padded_layout(rp.numpy(), world, chunks, balanced=balanced, row_cost=6,
+                                       rank_major=rank_major)
     truth = lay.pad_rows(torch.arange(n, dtype=torch.float32).unsqueeze(1) + 1.0)
     ids_of = lay.ids
     bufs = []
