@@ -85,6 +85,9 @@ def parse_args():
     ap.add_argument("--push-ctas", type=int, default=0, help="grid of the halo push kernel (0: the library default, 1 per SM)")
     ap.add_argument("--layout", choices=["balanced", "contiguous"], default="balanced",
                     help="N > 1: rows dealt to ranks by cost, or contiguous cost-balanced ranges")
+    ap.add_argument("--long-rows", choices=["shard", "graph"], default="shard",
+                    help="N > 1: long-row threshold of a 1/N share of the graph (every shard call), or the whole "
+                         "graph's (the one-GPU forward's bits; slower shards)")
     ap.add_argument("--padded-order", choices=["rank", "chunk"], default="rank",
                     help="N > 1 with pushes: every rank's rows one block of the exchange matrix (the last layer "
                          "then runs as one call), or piece-major blocks (the all_gather exchange always uses these)")
@@ -271,9 +274,11 @@ def run_ours(args, rank: int, world: int, device: torch.device):
         shard = partition.make_padded_shard(prob["rp"], prob["ci"], layout, rank)
         if args.exchange == "halo":
             halo = partition.make_halo_plan(prob["rp"], prob["ci"], layout, rank)
-        # every rank sums its rows with the whole graph's long-row threshold, as one GPU
-        # does, so the partitioned forward gives the one-GPU forward's bits
-        N.config_set("spmm.long_row_threshold", int(N.lib().gnn_spmm_long_row_threshold(n, nnz)))
+        # one long-row threshold for every call on every rank: the automatic value of a
+        # 1/N share of the graph (or the whole graph's); a row's sum depends only on it,
+        # so the output equals the one-GPU forward run at the same threshold, bit for bit
+        share = (-(-n // world), -(-nnz // world)) if args.long_rows == "shard" else (n, nnz)
+        N.config_set("spmm.long_row_threshold", int(N.lib().gnn_spmm_long_row_threshold(*share)))
         if args.check:
             whole_graph = {k: prob[k] for k in ("rp", "ci", "dis", "x")}
         prob["dis"] = layout.pad_rows(prob["dis"])
@@ -325,12 +330,18 @@ def run_ours(args, rank: int, world: int, device: torch.device):
     torch.cuda.synchronize(device)
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
+    step_ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
     with ClockSampler(device.index) as clocks:
         t_start.record()
-        for _ in range(args.steps):
+        h0 = time.perf_counter()
+        for i in range(args.steps):
+            step_ev[i].record()
             step(timers)
+        step_ev[-1].record()
+        host_ms = (time.perf_counter() - h0) * 1e3  # the host's time to issue the steps
         t_end.record()
         torch.cuda.synchronize(device)
+    step_ms = [a.elapsed_time(b) for a, b in zip(step_ev[:-1], step_ev[1:])]
     if world > 1:
         dist.barrier()
     launches = N.lib().gnn_kernel_launches() - launches0
@@ -451,7 +462,8 @@ def run_ours(args, rank: int, world: int, device: torch.device):
     # ---- reduce over ranks ----
     # per-layer algorithmic bytes of this rank's aggregation (its rows, its CSR entries)
     shard_bytes = spmm_layer_bytes(rows, shard.num_edges, FEAT)
-    vals = torch.tensor([ms_total, e2e_ms, spmm_ms_avg, float(launches), float(shard_bytes), xchg_ms],
+    vals = torch.tensor([ms_total, e2e_ms, spmm_ms_avg, float(launches), float(shard_bytes), xchg_ms,
+                         host_ms / args.steps, statistics.median(step_ms), max(step_ms), min(step_ms)],
                         dtype=torch.float64, device=device)
     per_rank = [vals.clone() for _ in range(world)]
     if world > 1:
@@ -499,6 +511,12 @@ def run_ours(args, rank: int, world: int, device: torch.device):
                      "spmm_ms_per_rank": [round(float(v), 4) for v in table[:, 2]],
                      "exchange_wait_ms_per_step_per_rank": [round(float(v), 4) for v in table[:, 5]],
                      "step_timeline_ms_per_rank": trace},
+        "steps_per_rank": {"host_issue_ms_per_step": [round(float(v), 4) for v in table[:, 6]],
+                           "gpu_ms_median": [round(float(v), 4) for v in table[:, 7]],
+                           "gpu_ms_max": [round(float(v), 4) for v in table[:, 8]],
+                           "gpu_ms_min": [round(float(v), 4) for v in table[:, 9]],
+                           "note": "per timed step on each rank: the host's time to issue it, and the device time "
+                                   "between events at step boundaries on the compute stream"},
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h), "ms_per_step": round(e2e_ms / args.e2e_steps, 3),
                 "copies": ("overlapped across steps (two input sets and two output buffers; inputs up / output "
@@ -612,9 +630,9 @@ def check_forward_sample(prob, h1: torch.Tensor, agg2: torch.Tensor, out: torch.
 def check_partitioned_forward(graph: dict, ws, bs, layout, rank: int, rows_out: torch.Tensor, device) -> dict:
     """This rank's output rows of the partitioned forward against the same rows
     of the one-GPU forward (the reference-facing calls over the whole graph, on
-    this rank's GPU), bit for bit; the count of differing rows is summed over
-    ranks. The one-GPU forward is itself checked against the oracle by the N = 1
-    line."""
+    this rank's GPU, at the long-row threshold the shards use), bit for bit; the
+    count of differing rows is summed over ranks. The one-GPU forward is itself
+    checked against the oracle by the N = 1 line."""
     agg = torch.empty(graph["x"].shape, device=device)
     h = graph["x"]
     for li in range(LAYERS):
@@ -630,7 +648,7 @@ def check_partitioned_forward(graph: dict, ws, bs, layout, rank: int, rows_out: 
     return {"rows_checked": total, "rows_differing": differ, "ok": differ == 0,
             "long_row_threshold": int(N.config_get("spmm.long_row_threshold")),
             "checked": "every output row of the partitioned forward (one extra step after the timed region) "
-                       "against the one-GPU forward of the whole graph, bit for bit"}
+                       "against the one-GPU forward of the whole graph at the same long-row threshold, bit for bit"}
 
 
 # ---------------------------------------------------------------------------
