@@ -85,6 +85,8 @@ def parse_args():
     ap.add_argument("--push-ctas", type=int, default=0, help="grid of the halo push kernel (0: the library default, 1 per SM)")
     ap.add_argument("--layout", choices=["balanced", "contiguous"], default="balanced",
                     help="N > 1: rows dealt to ranks by cost, or contiguous cost-balanced ranges")
+    ap.add_argument("--no-graphs", dest="graphs", action="store_false",
+                    help="N > 1: issue every step from Python instead of replaying it as a captured CUDA graph")
     ap.add_argument("--long-rows", choices=["shard", "graph"], default="shard",
                     help="N > 1: long-row threshold of a 1/N share of the graph (every shard call), or the whole "
                          "graph's (the one-GPU forward's bits; slower shards)")
@@ -323,6 +325,25 @@ def run_ours(args, rank: int, world: int, device: torch.device):
         step()
     torch.cuda.synchronize(device)
 
+    # N > 1: the step captured as CUDA graphs (one launch per step), when every rank captured it
+    graphs, graph_note = None, None
+    launches_per_step = None
+    if world > 1 and exchange is not None and args.graphs:
+        l0 = N.lib().gnn_kernel_launches()
+        try:
+            graphs = partition.PushForwardGraphs(step, exchange)
+        except Exception as e:  # noqa: BLE001 - reported, and every rank then runs eagerly
+            graphs, graph_note = None, f"capture failed: {type(e).__name__}: {str(e)[:200]}"
+        launches_per_step = (N.lib().gnn_kernel_launches() - l0) / 2
+        ok = torch.tensor([1 if graphs is not None else 0], device=device)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        if int(ok.item()) == 0 and graphs is not None:
+            graphs.close()
+            graphs, graph_note = None, "another rank's capture failed"
+        for _ in range(2 * max(1, args.warmup // 2) if graphs is not None else 0):
+            graphs.replay()
+        torch.cuda.synchronize(device)
+
     timers: dict = {}
     launches0 = N.lib().gnn_kernel_launches()
     if world > 1:
@@ -336,7 +357,10 @@ def run_ours(args, rank: int, world: int, device: torch.device):
         h0 = time.perf_counter()
         for i in range(args.steps):
             step_ev[i].record()
-            step(timers)
+            if graphs is not None:
+                graphs.replay()
+            else:
+                step(timers)
         step_ev[-1].record()
         host_ms = (time.perf_counter() - h0) * 1e3  # the host's time to issue the steps
         t_end.record()
@@ -345,7 +369,25 @@ def run_ours(args, rank: int, world: int, device: torch.device):
     if world > 1:
         dist.barrier()
     launches = N.lib().gnn_kernel_launches() - launches0
+    if graphs is not None:
+        # replays launch without the host counting them: the kernels each captured step holds
+        launches = int(round(launches_per_step * args.steps))
     ms_total = t_start.elapsed_time(t_end)
+    eager_ms = None
+    if graphs is not None:
+        # the per-phase figures (aggregation per rank, exchange wait) from eager steps,
+        # which carry the timing events that graph replays do not record
+        phase_steps = min(args.steps, 10)
+        torch.cuda.synchronize(device)
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(phase_steps):
+            step(timers)
+        e1.record()
+        torch.cuda.synchronize(device)
+        eager_ms = e0.elapsed_time(e1) / phase_steps
+    timed_steps = min(args.steps, 10) if graphs is not None else args.steps  # the steps the timers saw
     trace = None
     if world > 1 and args.exchange in ("push", "halo"):
         # one more step with a timeline of its phases on every rank (not part of the timed steps)
@@ -367,10 +409,15 @@ def run_ours(args, rank: int, world: int, device: torch.device):
         torch.cuda.empty_cache()
     # SpMM time per layer on this rank (summed over its row pieces when N > 1)
     spmm_ms = [b.elapsed_time(e) for b, e in timers.get("spmm", [])]
-    agg_calls = len(spmm_ms) // max(1, args.steps)
-    spmm_ms_avg = sum(spmm_ms) / max(1, args.steps * LAYERS)
+    agg_calls = len(spmm_ms) // max(1, timed_steps)
+    host_calls = {k: round(v * 1e3 / max(1, timed_steps), 4) for k, v in timers.get("host", {}).items()}
+    if world > 1:
+        everyone_host: list = [None] * world
+        dist.all_gather_object(everyone_host, host_calls)
+        host_calls = everyone_host
+    spmm_ms_avg = sum(spmm_ms) / max(1, timed_steps * LAYERS)
     # exposed exchange: how long the compute stream waits at each layer boundary
-    xchg_ms = sum(b.elapsed_time(e) for b, e in timers.get("xchg", [])) / max(1, args.steps)
+    xchg_ms = sum(b.elapsed_time(e) for b, e in timers.get("xchg", [])) / max(1, timed_steps)
 
     # ---- e2e through the public API with host buffers ----
     # every step copies this rank's inputs (its CSR rows, the normalisation vector,
@@ -463,7 +510,8 @@ def run_ours(args, rank: int, world: int, device: torch.device):
     # per-layer algorithmic bytes of this rank's aggregation (its rows, its CSR entries)
     shard_bytes = spmm_layer_bytes(rows, shard.num_edges, FEAT)
     vals = torch.tensor([ms_total, e2e_ms, spmm_ms_avg, float(launches), float(shard_bytes), xchg_ms,
-                         host_ms / args.steps, statistics.median(step_ms), max(step_ms), min(step_ms)],
+                         host_ms / args.steps, statistics.median(step_ms), max(step_ms), min(step_ms),
+                         eager_ms if eager_ms is not None else 0.0],
                         dtype=torch.float64, device=device)
     per_rank = [vals.clone() for _ in range(world)]
     if world > 1:
@@ -478,6 +526,8 @@ def run_ours(args, rank: int, world: int, device: torch.device):
     ms_step = ms_total / args.steps
     value = bytes_step / (ms_step * 1e-3) / 1e9
     e2e_value = bytes_step / ((e2e_ms / args.e2e_steps) * 1e-3) / 1e9
+    if graphs is not None:
+        graphs.close()  # graphs holding the barrier collective go before the exchange and the process group
     if exchange is not None:
         exchange.close()
 
@@ -515,6 +565,7 @@ def run_ours(args, rank: int, world: int, device: torch.device):
                            "gpu_ms_median": [round(float(v), 4) for v in table[:, 7]],
                            "gpu_ms_max": [round(float(v), 4) for v in table[:, 8]],
                            "gpu_ms_min": [round(float(v), 4) for v in table[:, 9]],
+                           "host_issue_ms_by_call": host_calls or None,
                            "note": "per timed step on each rank: the host's time to issue it, and the device time "
                                    "between events at step boundaries on the compute stream"},
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": int(h2d),
@@ -528,6 +579,14 @@ def run_ours(args, rank: int, world: int, device: torch.device):
         "gpu_launches": int(launches),
         "clocks": clocks.summary(),
     }
+    if world > 1 and exchange is not None:
+        result["cuda_graphs"] = {
+            "used": graphs is not None, "note": graph_note,
+            "kernels_per_step": launches_per_step,
+            "eager_ms_per_step": round(float(table[:, 10].max()), 4) if graphs is not None else None,
+            "how": "each step is one replay of a captured graph (two graphs, one per exchange copy, replayed in "
+                   "turn); gpu_launches = the kernels a captured step holds x steps; the per-phase figures come "
+                   "from min(steps, 10) eager steps after the timed ones, whose time is eager_ms_per_step"}
     if parity is not None:
         result["parity"] = parity
     if world == 1 and args.reference_gpu:

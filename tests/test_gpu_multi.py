@@ -73,7 +73,7 @@ def _worker(rank, world, port, q):
         cases = [("allgather", None, 1, False, False), ("allgather", None, 3, True, False),
                  ("push", "sm", 1, True, False), ("push", "ce", 3, True, False), ("push", "sm", 2, False, False),
                  ("halo", "sm", 1, True, False), ("halo", "sm", 2, True, False), ("halo", "sm", 3, False, False),
-                 ("halo", "sm", 2, True, True), ("push", "sm", 3, False, True)]
+                 ("halo", "sm", 2, True, True), ("push", "sm", 3, False, True), ("halo-graph", "sm", 2, True, True)]
         for how, transport, chunks, balanced, rank_major in cases:
             lay = partition.make_padded_layout(rp_np, world, chunks, balanced=balanced, row_cost=6,
                                                rank_major=rank_major)
@@ -84,11 +84,22 @@ def _worker(rank, world, port, q):
                 pout = partition.gcn_forward_allgather(pshard, dis_p, x_p, ws, bs, lay, pbufs)
             else:
                 ex = partition.PeerRowExchange(lay.padded_rows, FEAT, rank, world, dev, transport=transport)
-                halo = partition.make_halo_plan(rp, ci, lay, rank) if how == "halo" else None
+                halo = partition.make_halo_plan(rp, ci, lay, rank) if how.startswith("halo") else None
                 agg = torch.empty(lay.local_rows if rank_major else lay.chunk_rows, FEAT, device=dev)
                 mine = torch.empty(lay.local_rows, FEAT, device=dev)
+
+                def fwd():
+                    return partition.gcn_forward_push(pshard, dis_p, x_p, ws, bs, lay, ex, agg, mine, halo=halo)
                 for _ in range(3):  # repeated steps alternate the two copies
-                    pout = partition.gcn_forward_push(pshard, dis_p, x_p, ws, bs, lay, ex, agg, mine, halo=halo)
+                    pout = fwd()
+                if how == "halo-graph":
+                    # captured steps replayed in turn, with an eager step between replays
+                    mine.fill_(float("nan"))
+                    graphs = partition.PushForwardGraphs(fwd, ex)
+                    for k in range(5):
+                        pout = graphs.replay() if k != 2 else fwd()
+                    torch.cuda.synchronize(dev)
+                    graphs.close()
             # collect the final rows through the same layout
             pfull = torch.zeros(lay.local_rows, FEAT, device=dev)
             pfull[:pshard.num_rows] = pout
@@ -101,7 +112,7 @@ def _worker(rank, world, port, q):
                     dist.all_gather_into_tensor(gathered[c * world * mc:(c + 1) * world * mc],
                                                 pfull[c * mc:(c + 1) * mc])
             padded.append(lay.unpad_rows(gathered).cpu().numpy())
-            if how in ("push", "halo"):
+            if how != "allgather":
                 ex.close()
         torch.cuda.synchronize(dev)
         q.put((rank, full.cpu().numpy(), padded))

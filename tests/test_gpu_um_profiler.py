@@ -90,8 +90,12 @@ def test_profile_spmm_migration_reports_feature_range_traffic(tmp_path, ft_matri
     vals = _summary(res.stdout)
     feature_bytes = n * 256 * 4
     assert vals["spmm_ns"] > 0
-    if "nvidia-uvm-tools" in res.stderr:  # no counters on this system: the SpMM time is still reported
-        assert np.isnan(vals["HtoD_bytes"]) and np.isnan(vals["GPU_faults"])
+    if "nvidia-uvm-tools" in res.stderr:
+        # no unified-memory counters on this system: the SpMM time is still reported, the fault
+        # count is nan, and the bytes come from NVML's host-link counters (the whole device's
+        # PCIe bytes per iteration of the measured loop) when NVML answers, else nan
+        assert np.isnan(vals["GPU_faults"])
+        assert np.isnan(vals["HtoD_bytes"]) or vals["HtoD_bytes"] >= 0
     else:
         assert vals["HtoD_bytes"] >= 0.5 * feature_bytes  # the features are initialised on the host side
         if prefetch == 0:
