@@ -404,7 +404,8 @@ def run_ours(args, rank: int, world: int, device: torch.device):
         # the last timed step left h1 in out0, the layer-2 aggregate in agg, the output in out1
         parity = check_forward_sample(prob, bufs["out0"], bufs["agg"], bufs["out1"], device)
     elif args.check:
-        parity = check_partitioned_forward(whole_graph, prob["ws"], prob["bs"], layout, rank, step(), device)
+        rows_out = graphs.replay() if graphs is not None else step()  # what the timed steps ran
+        parity = check_partitioned_forward(whole_graph, prob["ws"], prob["bs"], layout, rank, rows_out, device)
         del whole_graph
         torch.cuda.empty_cache()
     # SpMM time per layer on this rank (summed over its row pieces when N > 1)
@@ -706,7 +707,8 @@ def check_partitioned_forward(graph: dict, ws, bs, layout, rank: int, rows_out: 
     differ, total = (int(v) for v in counts.cpu())
     return {"rows_checked": total, "rows_differing": differ, "ok": differ == 0,
             "long_row_threshold": int(N.config_get("spmm.long_row_threshold")),
-            "checked": "every output row of the partitioned forward (one extra step after the timed region) "
+            "checked": "every output row of the partitioned forward (one extra step after the timed region, "
+                       "a graph replay when the timed steps were replays) "
                        "against the one-GPU forward of the whole graph at the same long-row threshold, bit for bit"}
 
 
