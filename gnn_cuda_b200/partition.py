@@ -680,12 +680,13 @@ class PushForwardGraphs:
         self.graphs = []
         self.out = None
         for _ in range(2):
+            before = exchange.turn
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, capture_error_mode="thread_local"):
                 self.out = step_fn()
             self.graphs.append(g)
-        if exchange.turn != self.first_turn:
-            raise RuntimeError("a captured step must finish exactly one exchange")
+            if exchange.turn != before ^ 1:
+                raise RuntimeError("a captured step must finish exactly one exchange")
 
     def replay(self) -> torch.Tensor:
         self.graphs[self.exchange.turn ^ self.first_turn].replay()
