@@ -679,14 +679,20 @@ class PushForwardGraphs:
         self.first_turn = exchange.turn
         self.graphs = []
         self.out = None
-        for _ in range(2):
-            before = exchange.turn
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, capture_error_mode="thread_local"):
-                self.out = step_fn()
-            self.graphs.append(g)
-            if exchange.turn != before ^ 1:
-                raise RuntimeError("a captured step must finish exactly one exchange")
+        try:
+            for _ in range(2):
+                before = exchange.turn
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, capture_error_mode="thread_local"):
+                    self.out = step_fn()
+                self.graphs.append(g)
+                if exchange.turn != before ^ 1:
+                    raise RuntimeError("a captured step must finish exactly one exchange")
+        except Exception:
+            # every rank must go on from the same copy, whether its capture failed or not
+            exchange.turn = self.first_turn
+            self.graphs = []
+            raise
 
     def replay(self) -> torch.Tensor:
         self.graphs[self.exchange.turn ^ self.first_turn].replay()

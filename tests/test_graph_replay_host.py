@@ -80,3 +80,20 @@ def test_a_step_that_does_not_finish_one_exchange_is_refused(monkeypatch):
     _fakes(monkeypatch, ex, [])
     with pytest.raises(RuntimeError, match="exactly one exchange"):
         partition.PushForwardGraphs(lambda: "rows", ex)  # never moves to the other copy
+
+
+def test_a_failed_capture_leaves_the_exchange_on_its_first_copy(monkeypatch):
+    """Ranks whose capture failed go on eagerly with the others: all from the same copy."""
+    ex = _Exchange(1)
+    _fakes(monkeypatch, ex, [])
+    calls = []
+
+    def step():
+        calls.append(ex.turn)
+        ex.turn ^= 1  # the exchange moved on before the failure
+        if len(calls) == 2:
+            raise RuntimeError("operation not permitted when stream is capturing")
+        return "rows"
+    with pytest.raises(RuntimeError, match="capturing"):
+        partition.PushForwardGraphs(step, ex)
+    assert ex.turn == 1
