@@ -85,6 +85,9 @@ def parse_args():
     ap.add_argument("--push-ctas", type=int, default=0, help="grid of the halo push kernel (0: the library default, 1 per SM)")
     ap.add_argument("--layout", choices=["balanced", "contiguous"], default="balanced",
                     help="N > 1: rows dealt to ranks by cost, or contiguous cost-balanced ranges")
+    ap.add_argument("--push-from", choices=["kernel", "transform"], default="kernel",
+                    help="N > 1 halo exchange: a push kernel after the transform, or the transform's epilogue "
+                         "storing the halo rows to the peers itself (gnn_linear_push_forward)")
     ap.add_argument("--no-graphs", dest="graphs", action="store_false",
                     help="N > 1: issue every step from Python instead of replaying it as a captured CUDA graph")
     ap.add_argument("--long-rows", choices=["shard", "graph"], default="shard",
@@ -236,7 +239,7 @@ def default_chunks(chunks: int, world: int) -> int:
 
 def describe(prob, world: int, gemm: str | None = None, chunks: int = 1, exchange: str = "halo",
              transport: str = "sm", layout: str = "balanced", order: str | None = None,
-             padded_order: str = "rank") -> dict:
+             padded_order: str = "rank", push_from: str = "kernel") -> dict:
     if gemm is None:
         gemm = "tcgen05-tf32" if N.lib().gnn_gemm_uses_tensor_cores(prob["n"], FEAT, FEAT) else "ffma-fp32"
     if order is None:
@@ -248,6 +251,7 @@ def describe(prob, world: int, gemm: str | None = None, chunks: int = 1, exchang
                                              f"+{layout}_{transport}_push_pieces{chunks}_{padded_order}_major"
                                              if exchange == "push" else
                                              f"+{layout}_halo_push_pieces{chunks}_{padded_order}_major"
+                                             + ("_from_transform" if push_from == "transform" else "")
                                              if exchange == "halo" else
                                              f"+{layout}_nccl_allgather_pieces{chunks}"),
             "l2": "inputs larger than L2 (X is %.2f GB), no flush" % (prob["n"] * FEAT * 4 / 1e9),
@@ -265,6 +269,7 @@ def run_ours(args, rank: int, world: int, device: torch.device):
     rp_cpu = prob["rp"].to(torch.int64).cpu().numpy()
     exchange = None
     halo = None
+    push_masks = None
     args.chunks = default_chunks(args.chunks, world)
     if world == 1:
         shard = partition.make_shard(prob["rp"], prob["ci"], 0, n)
@@ -279,6 +284,8 @@ def run_ours(args, rank: int, world: int, device: torch.device):
         shard = partition.make_padded_shard(prob["rp"], prob["ci"], layout, rank)
         if args.exchange == "halo":
             halo = partition.make_halo_plan(prob["rp"], prob["ci"], layout, rank)
+            if args.push_from == "transform":
+                push_masks = halo.piece_masks(shard)
         # one long-row threshold for every call on every rank: the automatic value of a
         # 1/N share of the graph (or the whole graph's); a row's sum depends only on it,
         # so the output equals the one-GPU forward run at the same threshold, bit for bit
@@ -320,7 +327,7 @@ def run_ours(args, rank: int, world: int, device: torch.device):
         if args.exchange in ("push", "halo"):
             return partition.gcn_forward_push(shard, prob["dis"], prob["x"], prob["ws"], prob["bs"], layout, exchange,
                                               bufs["agg"], bufs["out"] if final_out is None else final_out,
-                                              timers=timers, halo=halo)
+                                              timers=timers, halo=halo, push_masks=push_masks)
         return partition.gcn_forward_allgather(shard, prob["dis"], prob["x"], prob["ws"], prob["bs"], layout, bufs,
                                                timers=timers)
 
@@ -396,7 +403,7 @@ def run_ours(args, rank: int, world: int, device: torch.device):
         # one more step with a timeline of its phases on every rank (not part of the timed steps)
         ev_list: list = []
         partition.gcn_forward_push(shard, prob["dis"], prob["x"], prob["ws"], prob["bs"], layout, exchange,
-                                   bufs["agg"], bufs["out"], halo=halo, trace=ev_list)
+                                   bufs["agg"], bufs["out"], halo=halo, trace=ev_list, push_masks=push_masks)
         torch.cuda.synchronize(device)
         trace = partition.trace_offsets(ev_list)
         everyone: list = [None] * world
@@ -557,7 +564,7 @@ def run_ours(args, rank: int, world: int, device: torch.device):
         "data": f"synthetic: seeded R-MAT graph (seed {args.seed}) with ogbn-products shape, N(0,1) features, "
                 "Glorot weights, zero bias",
         "config": describe(prob, world, chunks=args.chunks, exchange=args.exchange, transport=args.transport,
-                           layout=args.layout, padded_order=args.padded_order),
+                           layout=args.layout, padded_order=args.padded_order, push_from=args.push_from),
         "roofline": {"bound": "hbm", "kernel": "spmm_vec_kernel + spmm_long_kernel (GCN aggregation)",
                      "achieved": round(achieved, 1) if achieved else None, "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4) if achieved else None, "peak_source": peak_kind,
@@ -882,7 +889,7 @@ def run_reference(args):
     hp = _host_problem(prob)
     cfg = describe(prob, args.gpus, gemm="cpu-fp32", order="CSR row order (C restatement, OpenMP over rows)",
                    chunks=default_chunks(args.chunks, args.gpus), exchange=args.exchange, transport=args.transport,
-                   layout=args.layout, padded_order=args.padded_order)
+                   layout=args.layout, padded_order=args.padded_order, push_from=args.push_from)
     del prob
     threads = O.max_threads()
     total = args.steps + args.warmup

@@ -327,6 +327,32 @@ def linear_forward_(x, weight, bias, out, relu=False, precision: int | None = No
                x.size(1), weight.size(1), int(bool(relu)), p, _stream(out.device))
 
 
+def linear_push_forward_(x, weight, bias, out, relu, peer_mask, peer_rows: list[int]) -> bool:
+    """linear_forward_ (TF32 tensor-core path) that also stores every output row i to
+    row i of peer_rows[d] (device addresses of the same [m, n] rows in peers' buffers)
+    for each bit d of peer_mask[i] (uint8, one per row), from the GEMM's epilogue.
+    Returns False, having launched nothing, where the tensor-core GEMM does not apply;
+    the caller then runs linear_forward_ and a separate push."""
+    _check_gemm(x, weight, out)
+    _check_bias(bias, out)
+    _check(peer_mask.is_cuda and peer_mask.dtype == torch.uint8 and peer_mask.is_contiguous(),
+           "peer_mask must be a contiguous CUDA uint8 tensor")
+    _check(peer_mask.numel() == out.size(0), "peer_mask needs one entry per output row")
+    _check(len(peer_rows) <= 8, "at most 8 peers")
+    if gemm_precision() != N.GNN_PRECISION_TF32:
+        return False
+    arr = (ctypes.c_void_p * max(1, len(peer_rows)))(*peer_rows)
+    with torch.cuda.device(out.device):
+        rc = N.lib().gnn_linear_push_forward(_dev_ptr(x), _dev_ptr(weight), _dev_ptr(bias), out.data_ptr(),
+                                             x.size(0), x.size(1), weight.size(1), int(bool(relu)),
+                                             peer_mask.data_ptr() if peer_mask.numel() else None, arr,
+                                             len(peer_rows), _stream(out.device))
+    if rc == N.GNN_ERR_UNSUPPORTED:
+        return False
+    N.check(rc, "gnn_linear_push_forward")
+    return True
+
+
 def bias_relu_forward_(out, bias, relu=False):
     """agg_ops.cu:393 (checks :282-295)."""
     _check(out.is_cuda, "out must be CUDA")

@@ -16,6 +16,7 @@ _PKG = Path(__file__).resolve().parent
 LIB_PATH = Path(os.environ.get("GNNB200_LIB", _PKG / "libgnnb200.so"))
 
 GNN_OK = 0
+GNN_ERR_UNSUPPORTED = 3
 GNN_AGG_GCN, GNN_AGG_SUM, GNN_AGG_MEAN, GNN_AGG_MEAN_RECIPROCAL = 0, 1, 2, 3
 GNN_INDEX_INT32, GNN_INDEX_INT64 = 0, 1
 GNN_PRECISION_TF32, GNN_PRECISION_FP32 = 0, 1
@@ -71,6 +72,7 @@ PROTOTYPES: dict[str, tuple[object, list[object]]] = {
                _vp, _i64, _i32, _vp, _vp, _sz, _vp]),
     "gnn_gemm_forward": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i32, _vp]),
     "gnn_linear_forward": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _i32, _vp]),
+    "gnn_linear_push_forward": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _vp, _vp, _i32, _vp]),
     "gnn_bias_relu_forward": (_i32, [_vp, _vp, _i64, _i64, _i32, _vp]),
     "gnn_tensor_add_inplace": (_i32, [_vp, _vp, _f32, _i64, _vp]),
     "gnn_relu_inplace": (_i32, [_vp, _i64, _vp]),

@@ -49,6 +49,8 @@ constexpr int OUT_STAGING_BYTES = 4 * 2 * OUT_BLOCK_BYTES;  // 4 epilogue warps 
 // device status word: 0 ok, otherwise the role that gave up waiting
 __device__ int g_tc_status = 0;
 
+constexpr int kMaxPeers = 8;  // destinations of the fused halo push
+
 struct TcParams {
   int64_t m, k, n;
   int64_t m_tiles;
@@ -57,11 +59,16 @@ struct TcParams {
   float* out;
   int relu;
   int stages;  // X chunk ring depth (2..MAX_STAGES)
+  // fused halo push (PUSH instantiation only): output row i also goes to row i of
+  // peer_out[q] for every bit q set in peer_mask[i]
+  const uint8_t* peer_mask;
+  float* peer_out[kMaxPeers];
+  int npeers;
 };
 
 __device__ __forceinline__ void record_timeout(int code) { atomicCAS(&g_tc_status, 0, code); }
 
-template <int BN>
+template <int BN, bool PUSH>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tf32_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_out,
                         const float* __restrict__ w, TcParams p) {
@@ -228,6 +235,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int64_t row0 = mt * BM + 32 * q;  // first row of this warp's lane quarter
       const bool has_rows = row0 < p.m;        // rows past m are clipped by the store
+      // PUSH: the peers that read this lane's row (none for rows past m)
+      uint32_t my_mask = 0;
+      if (PUSH && row0 + lane < p.m) my_mask = __ldg(p.peer_mask + row0 + lane);
+      const bool any_push = PUSH && __any_sync(0xffffffffu, my_mask != 0);
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
         uint32_t r[32];
@@ -256,6 +267,25 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (lane == 0) {
             tma_store_2d(&tmap_out, buf, ncol0 + c0, static_cast<int>(row0));
             bulk_commit();
+          }
+          if (any_push) {
+            // the block's rows that peers read, back out of the staging buffer in row
+            // order: 8 lanes per row (its 128 bytes of this column block), 4 rows a pass,
+            // each stored to every peer whose bit is set (plain stores over NVLink)
+            const int c = lane & 7;
+#pragma unroll 1
+            for (int pass = 0; pass < 8; ++pass) {
+              const int j = pass * 4 + (lane >> 3);
+              const uint32_t mj = __shfl_sync(0xffffffffu, my_mask, j);
+              if (mj != 0) {
+                const float4 v = *reinterpret_cast<const float4*>(buf + j * 128 + ((c ^ (j & 7)) << 4));
+                const int64_t off = (row0 + j) * p.n + ncol0 + c0 + c * 4;
+#pragma unroll
+                for (int d = 0; d < kMaxPeers; ++d) {
+                  if (d < p.npeers && ((mj >> d) & 1u)) *reinterpret_cast<float4*>(p.peer_out[d] + off) = v;
+                }
+              }
+            }
           }
           ++blocks;
         }
@@ -347,9 +377,9 @@ size_t smem_bytes(int bn, int64_t k) {
   return s ? smem_bytes_for(bn, k, s) : kSmemLimit + 1;
 }
 
-template <int BN>
+template <int BN, bool PUSH>
 int launch_bn(const float* x, const float* w, const float* bias, float* out, int64_t m, int64_t k, int64_t n,
-              bool relu, cudaStream_t stream) {
+              bool relu, const uint8_t* peer_mask, float* const* peer_out, int npeers, cudaStream_t stream) {
   EncodeTiledFn enc = encode_fn();
   if (enc == nullptr) return fail(GNN_ERR_DEVICE, "cuTensorMapEncodeTiled is not available from the driver");
   CUtensorMap tx{};
@@ -377,15 +407,15 @@ int launch_bn(const float* x, const float* w, const float* bias, float* out, int
   }
   const size_t smem = smem_bytes(BN, k);
   // the opt-in is a per-device function attribute; remember the largest size set per device
-  static int configured_smem[64][3] = {};
+  static int configured_smem[64][6] = {};
   static std::mutex mu;
   int dev = 0;
   GNN_CUDA_TRY(cudaGetDevice(&dev), "cudaGetDevice");
-  const int slot = BN == 128 ? 0 : (BN == 64 ? 1 : 2);
+  const int slot = (BN == 128 ? 0 : (BN == 64 ? 1 : 2)) + (PUSH ? 3 : 0);
   {
     std::lock_guard<std::mutex> lock(mu);
     if (dev < 0 || dev >= 64 || configured_smem[dev][slot] < static_cast<int>(smem)) {
-      GNN_CUDA_TRY(cudaFuncSetAttribute(gemm_tf32_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      GNN_CUDA_TRY(cudaFuncSetAttribute(gemm_tf32_tc_kernel<BN, PUSH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         static_cast<int>(smem)),
                    "gemm_tf32_tc_kernel: shared memory opt-in");
       if (dev >= 0 && dev < 64) configured_smem[dev][slot] = static_cast<int>(smem);
@@ -402,10 +432,13 @@ int launch_bn(const float* x, const float* w, const float* bias, float* out, int
   p.relu = relu ? 1 : 0;
   p.stages = stages_for(BN, k);
   if (p.stages < 2) return fail(GNN_ERR_UNSUPPORTED, "gemm_tf32_tc_kernel: shared memory too small for K");
+  p.peer_mask = peer_mask;
+  p.npeers = PUSH ? npeers : 0;
+  for (int d = 0; d < kMaxPeers; ++d) p.peer_out[d] = (PUSH && d < npeers) ? peer_out[d] : nullptr;
   const int64_t tiles = p.m_tiles * p.n_tiles;
   int64_t ctas = std::min<int64_t>(tiles, sm_count());
   ctas = std::max<int64_t>(p.n_tiles, (ctas / p.n_tiles) * p.n_tiles);
-  gemm_tf32_tc_kernel<BN><<<static_cast<unsigned>(ctas), kThreads, smem, stream>>>(tx, to, w, p);
+  gemm_tf32_tc_kernel<BN, PUSH><<<static_cast<unsigned>(ctas), kThreads, smem, stream>>>(tx, to, w, p);
   GNN_LAUNCH_CHECK("gemm_tf32_tc_kernel launch");
   return GNN_OK;
 }
@@ -426,12 +459,21 @@ int gemm_tc_tf32(const float* x, const float* w, const float* bias, float* out, 
   if (!gemm_tc_eligible(x, w, bias, out, m, k, n)) return GNN_OK;
   int rc;
   switch (pick_bn(n)) {
-    case 128: rc = launch_bn<128>(x, w, bias, out, m, k, n, relu, stream); break;
-    case 64: rc = launch_bn<64>(x, w, bias, out, m, k, n, relu, stream); break;
-    default: rc = launch_bn<32>(x, w, bias, out, m, k, n, relu, stream); break;
+    case 128: rc = launch_bn<128, false>(x, w, bias, out, m, k, n, relu, nullptr, nullptr, 0, stream); break;
+    case 64: rc = launch_bn<64, false>(x, w, bias, out, m, k, n, relu, nullptr, nullptr, 0, stream); break;
+    default: rc = launch_bn<32, false>(x, w, bias, out, m, k, n, relu, nullptr, nullptr, 0, stream); break;
   }
   if (rc == GNN_OK) *handled = true;
   return rc;
+}
+
+int gemm_tc_tf32_push(const float* x, const float* w, const float* bias, float* out, int64_t m, int64_t k, int64_t n,
+                      bool relu, const uint8_t* peer_mask, float* const* peer_out, int npeers, cudaStream_t stream) {
+  switch (pick_bn(n)) {
+    case 128: return launch_bn<128, true>(x, w, bias, out, m, k, n, relu, peer_mask, peer_out, npeers, stream);
+    case 64: return launch_bn<64, true>(x, w, bias, out, m, k, n, relu, peer_mask, peer_out, npeers, stream);
+    default: return launch_bn<32, true>(x, w, bias, out, m, k, n, relu, peer_mask, peer_out, npeers, stream);
+  }
 }
 
 int tc_status_read(int reset, int* status) {
@@ -458,6 +500,46 @@ extern "C" int gnn_device_status(int reset, int* status) {
   *status = tc != 0 ? tc : sp;
   gnnb200::clear_error();
   return GNN_OK;
+}
+
+extern "C" int gnn_linear_push_forward(const float* x, const float* weight, const float* bias, float* out,
+                                       int64_t m, int64_t k, int64_t n, int relu, const uint8_t* peer_mask,
+                                       float* const* peer_out, int npeers, gnn_stream_t stream) {
+  GNN_REQUIRE(m >= 0 && k >= 0 && n >= 0, GNN_ERR_INVALID_ARGUMENT, "m, k and n must be >= 0");
+  GNN_REQUIRE(npeers >= 0 && npeers <= gnnb200::kMaxPeers, GNN_ERR_INVALID_ARGUMENT,
+              "npeers must be in [0, 8]");
+  if (m == 0) {
+    gnnb200::clear_error();
+    return GNN_OK;
+  }
+  GNN_REQUIRE(x != nullptr && weight != nullptr && out != nullptr, GNN_ERR_NULL_POINTER,
+              "x, weight and out must not be NULL");
+  GNN_REQUIRE(npeers == 0 || (peer_mask != nullptr && peer_out != nullptr), GNN_ERR_NULL_POINTER,
+              "peer_mask and peer_out must not be NULL when npeers > 0");
+  uintptr_t a = 0;
+  for (int d = 0; d < npeers; ++d) {
+    GNN_REQUIRE(peer_out[d] != nullptr, GNN_ERR_NULL_POINTER, "peer_out entries must not be NULL");
+    a |= reinterpret_cast<uintptr_t>(peer_out[d]);
+  }
+  GNN_REQUIRE(a % 16 == 0 && (n * 4) % 16 == 0, GNN_ERR_INVALID_ARGUMENT,
+              "peer rows must be 16-byte aligned");
+  if (!gnnb200::gemm_tc_eligible(x, weight, bias, out, m, k, n)) {
+    return gnnb200::fail(GNN_ERR_UNSUPPORTED,
+                         "linear push: needs the TF32 tensor-core GEMM (sm_100, K a multiple of 32 up to 256, "
+                         "N in {32, 64} or a multiple of 128, 16-byte aligned operands)");
+  }
+  int rc;
+  if (npeers == 0) {  // nothing to push: the plain instantiation (the mask is never read)
+    bool handled = false;
+    rc = gnnb200::gemm_tc_tf32(x, weight, bias, out, m, k, n, relu != 0, reinterpret_cast<cudaStream_t>(stream),
+                               &handled);
+    if (rc == GNN_OK && !handled) rc = gnnb200::fail(GNN_ERR_UNSUPPORTED, "linear push: tensor-core GEMM not taken");
+  } else {
+    rc = gnnb200::gemm_tc_tf32_push(x, weight, bias, out, m, k, n, relu != 0, peer_mask, peer_out, npeers,
+                                    reinterpret_cast<cudaStream_t>(stream));
+  }
+  if (rc == GNN_OK) gnnb200::clear_error();
+  return rc;
 }
 
 extern "C" int gnn_gemm_uses_tensor_cores(int64_t m, int64_t k, int64_t n) {

@@ -346,6 +346,24 @@ class HaloPlan:
     def rows_sent(self) -> int:
         return sum(o[-1] for o in self.offsets)
 
+    def piece_masks(self, shard: "PaddedShard") -> list[torch.Tensor]:
+        """The same lists as one byte per row of each piece (uint8, on the ids'
+        device): bit q of row i is set when peers[q] reads row i of the piece.
+        This is the form the transform's fused push reads (gnn_linear_push_forward)."""
+        if self.peers and len(self.peers) > 8:
+            raise ValueError("a row mask holds at most 8 peers")
+        masks = []
+        for c, piece in enumerate(shard.pieces):
+            ids = self.ids[c]
+            m = torch.zeros(piece.num_rows, dtype=torch.uint8, device=ids.device)
+            off = self.offsets[c]
+            for q in range(len(self.peers)):
+                seg = ids[off[q]:off[q + 1]].to(torch.int64) - piece.row_begin
+                if seg.numel():
+                    m[seg] |= 1 << q
+            masks.append(m)
+        return masks
+
 
 def make_halo_plan(row_ptr: torch.Tensor, col_ind: torch.Tensor, layout: PaddedLayout, rank: int) -> HaloPlan:
     """Halo lists of `rank` from the global CSR (global ids, any device): every
@@ -569,10 +587,20 @@ class PeerRowExchange:
                ctypes.c_void_p(ids.data_ptr()), offs, self.row_bytes, self.shape[0], self.ctas,
                ctypes.c_void_p(s.cuda_stream))
 
+    def peer_rows(self, row_begin: int, peers: list[int]) -> list[int]:
+        """Device addresses of row `row_begin` of each peer's current copy (in `peers`
+        order), for a kernel on the compute stream that stores rows to the peers
+        itself (the fused push of the transform)."""
+        return [self.peer_ptrs[self.turn][p] + row_begin * self.row_bytes for p in peers]
+
     def finish(self) -> torch.Tensor:
-        """Barrier after every rank's pushes; returns the completed copy and moves to the other one."""
+        """Barrier after every rank's pushes; returns the completed copy and moves to the other one.
+
+        The barrier also follows the work issued so far on the calling stream, where a
+        fused push (rows stored to the peers by the transform itself) runs."""
         for s in self.streams.values():
             self.barrier_stream.wait_stream(s)
+        self.barrier_stream.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(self.barrier_stream):
             work = dist.all_reduce(self.flag, group=self.group, async_op=True)
         work.wait()  # the current (compute) stream waits for the barrier
@@ -598,7 +626,7 @@ class PeerRowExchange:
 def gcn_forward_push(shard: PaddedShard, dis_pad: torch.Tensor, x_pad: torch.Tensor, weights: list[torch.Tensor],
                      biases: list[torch.Tensor], layout: PaddedLayout, exchange: PeerRowExchange, agg: torch.Tensor,
                      out: torch.Tensor, timers: dict | None = None, halo: HaloPlan | None = None,
-                     trace: list | None = None) -> torch.Tensor:
+                     trace: list | None = None, push_masks: list[torch.Tensor] | None = None) -> torch.Tensor:
     """Multi-layer GCN over a padded-layout shard; layer outputs pushed to the peers piece by piece.
 
     exchange: a PeerRowExchange over layout.padded_rows rows. agg: [Mc, F]
@@ -609,7 +637,10 @@ def gcn_forward_push(shard: PaddedShard, dis_pad: torch.Tensor, x_pad: torch.Ten
     reads are pushed. The last layer pushes nothing, so when the shard's rows
     are one contiguous block (shard.whole) and agg holds them all it runs as
     one aggregation call and one transform: the same per-row sums as the
-    pieces, without a call per piece.
+    pieces, without a call per piece. With `push_masks` (halo.piece_masks(shard))
+    the transform stores the halo rows to the peers itself, from its epilogue
+    while later tiles are computed (gnn_linear_push_forward), instead of a push
+    kernel after it; where that kernel does not apply the separate push runs.
     Returns this rank's [rows, F] output rows (local order). With `trace`, a list,
     (label, event) pairs are appended for one step's timeline: the start, every
     piece's aggregation and transform end (compute stream), its push end (push
@@ -637,10 +668,14 @@ def gcn_forward_push(shard: PaddedShard, dis_pad: torch.Tensor, x_pad: torch.Ten
                 dst = out[c * mc:c * mc + piece.num_rows]
             else:
                 dst = exchange.buffer()[piece.row_begin:piece.row_end]
-            native_ops.linear_forward_(a, weights[li], biases[li], dst, not last)
+            fused = (not last and push_masks is not None and halo is not None and exchange.transport == "sm" and
+                     native_ops.linear_push_forward_(a, weights[li], biases[li], dst, True, push_masks[c],
+                                                     exchange.peer_rows(piece.row_begin, halo.peers)))
+            if not fused:
+                native_ops.linear_forward_(a, weights[li], biases[li], dst, not last)
             t0 = _host_time(timers, "transform", t0)
             _trace(trace, f"l{li}p{c}_gemm")
-            if not last:
+            if not last and not fused:
                 ready = torch.cuda.Event()
                 ready.record()
                 if halo is None:

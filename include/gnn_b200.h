@@ -252,6 +252,20 @@ int gnn_linear_forward(const float* x, const float* weight, const float* bias, f
                        int64_t m, int64_t k, int64_t n, int relu, int precision,
                        gnn_stream_t stream);
 
+/* gnn_linear_forward at GNN_PRECISION_TF32 on the tcgen05 path, fused with the
+ * halo push of the multi-GPU forward: output row i is also stored to row i of
+ * peer_out[d] (a peer's buffer from gnn_ipc_open, the same [m, n] layout) for
+ * every bit d set in peer_mask[i] (one byte per row, device memory), from the
+ * GEMM's epilogue while later tiles are still computed. npeers <= 8; peer rows
+ * 16-byte aligned. Returns GNN_ERR_UNSUPPORTED (nothing launched) where the
+ * tensor-core GEMM does not apply (gnn_gemm_uses_tensor_cores, 16-byte aligned
+ * operands); the caller then runs gnn_linear_forward and gnn_peer_push_rows.
+ * Replaces, for the multi-GPU mode (no reference counterpart), the pair
+ * linear_forward_cuda_ (agg_ops.cu:343) + gnn_peer_push_rows. */
+int gnn_linear_push_forward(const float* x, const float* weight, const float* bias, float* out,
+                            int64_t m, int64_t k, int64_t n, int relu, const uint8_t* peer_mask,
+                            float* const* peer_out, int npeers, gnn_stream_t stream);
+
 /* out[i, j] = relu?(out[i, j] + bias[j]); bias may be NULL.
  * Replaces bias_relu_forward_cuda_, agg_ops.cu:393 (kernel :132-147). */
 int gnn_bias_relu_forward(float* out, const float* bias, int64_t rows, int64_t cols, int relu,

@@ -73,7 +73,9 @@ def _worker(rank, world, port, q):
         cases = [("allgather", None, 1, False, False), ("allgather", None, 3, True, False),
                  ("push", "sm", 1, True, False), ("push", "ce", 3, True, False), ("push", "sm", 2, False, False),
                  ("halo", "sm", 1, True, False), ("halo", "sm", 2, True, False), ("halo", "sm", 3, False, False),
-                 ("halo", "sm", 2, True, True), ("push", "sm", 3, False, True), ("halo-graph", "sm", 2, True, True)]
+                 ("halo", "sm", 2, True, True), ("push", "sm", 3, False, True), ("halo-graph", "sm", 2, True, True),
+                 ("halo-fused", "sm", 1, True, True), ("halo-fused", "sm", 2, False, True),
+                 ("halo-fused-graph", "sm", 1, True, True)]
         for how, transport, chunks, balanced, rank_major in cases:
             lay = partition.make_padded_layout(rp_np, world, chunks, balanced=balanced, row_cost=6,
                                                rank_major=rank_major)
@@ -88,11 +90,17 @@ def _worker(rank, world, port, q):
                 agg = torch.empty(lay.local_rows if rank_major else lay.chunk_rows, FEAT, device=dev)
                 mine = torch.empty(lay.local_rows, FEAT, device=dev)
 
+                masks = None
+                if "fused" in how:  # the transform stores the halo rows to the peers itself
+                    assert N.lib().gnn_gemm_uses_tensor_cores(pshard.pieces[0].num_rows, FEAT, FEAT) == 1
+                    masks = halo.piece_masks(pshard)
+
                 def fwd():
-                    return partition.gcn_forward_push(pshard, dis_p, x_p, ws, bs, lay, ex, agg, mine, halo=halo)
+                    return partition.gcn_forward_push(pshard, dis_p, x_p, ws, bs, lay, ex, agg, mine, halo=halo,
+                                                      push_masks=masks)
                 for _ in range(3):  # repeated steps alternate the two copies
                     pout = fwd()
-                if how == "halo-graph":
+                if how.endswith("graph"):
                     # captured steps replayed in turn, with an eager step between replays
                     mine.fill_(float("nan"))
                     graphs = partition.PushForwardGraphs(fwd, ex)
