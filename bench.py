@@ -532,7 +532,7 @@ def run_ours(args, rank: int, world: int, device: torch.device):
     shard_bytes = spmm_layer_bytes(rows, shard.num_edges, FEAT)
     vals = torch.tensor([ms_total, e2e_ms, spmm_ms_avg, float(launches), float(shard_bytes), xchg_ms,
                          host_ms / args.steps, statistics.median(step_ms), max(step_ms), min(step_ms),
-                         eager_ms if eager_ms is not None else 0.0],
+                         eager_ms if eager_ms is not None else 0.0, float(step_ms.index(max(step_ms)))],
                         dtype=torch.float64, device=device)
     per_rank = [vals.clone() for _ in range(world)]
     if world > 1:
@@ -586,6 +586,7 @@ def run_ours(args, rank: int, world: int, device: torch.device):
                            "gpu_ms_median": [round(float(v), 4) for v in table[:, 7]],
                            "gpu_ms_max": [round(float(v), 4) for v in table[:, 8]],
                            "gpu_ms_min": [round(float(v), 4) for v in table[:, 9]],
+                           "gpu_ms_max_step_index": [int(v) for v in table[:, 11]],
                            "host_issue_ms_by_call": host_calls or None,
                            "note": "per timed step on each rank: the host's time to issue it, and the device time "
                                    "between events at step boundaries on the compute stream"},
