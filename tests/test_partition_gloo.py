@@ -302,3 +302,30 @@ def test_halo_plan_delivers_every_row_a_rank_reads(world, chunks, balanced, rank
         own = set(ids_of[lay.order[r]].tolist())
         sent += len(set(cols.tolist()) - own)
     assert sent == sum(p.rows_sent for p in plans)
+
+
+@pytest.mark.parametrize("world,chunks,rank_major", [(2, 1, True), (4, 3, True), (8, 2, False), (8, 1, True)])
+def test_halo_piece_masks_hold_the_halo_lists(world, chunks, rank_major):
+    """Bit q of row i of piece c's mask is set exactly when peers[q]'s list holds that row:
+    the form the transform's fused push reads."""
+    n = 2500
+    u, v = synth.rmat_undirected(n, n * 5, seed=world * 10 + chunks)
+    s, d = synth.symmetrize(u, v)
+    rp, ci, _ = synth.csr_on_device(s, d, n, add_self_loops=True)
+    lay = partition.make_padded_layout(rp.numpy(), world, chunks, balanced=True, row_cost=6, rank_major=rank_major)
+    for r in range(world):
+        plan = partition.make_halo_plan(rp, ci, lay, r)
+        shard = partition.make_padded_shard(rp, ci, lay, r)
+        masks = plan.piece_masks(shard)
+        assert len(masks) == len(shard.pieces)
+        for c, (piece, m) in enumerate(zip(shard.pieces, masks)):
+            assert m.dtype == torch.uint8 and m.numel() == piece.num_rows
+            want = torch.zeros(piece.num_rows, dtype=torch.int64)
+            off = plan.offsets[c]
+            for q in range(len(plan.peers)):
+                rows = plan.ids[c][off[q]:off[q + 1]].to(torch.int64) - piece.row_begin
+                assert bool(((rows >= 0) & (rows < piece.num_rows)).all())
+                want[rows] |= 1 << q
+            assert torch.equal(m.to(torch.int64), want)
+        assert sum(int(torch.bitwise_and(mk.to(torch.int64)[:, None], 1 << torch.arange(8)).ne(0).sum())
+                   for mk in masks) == plan.rows_sent
