@@ -148,12 +148,15 @@ class ClockSampler:
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
+    def __init__(self, gpu_index: int, enabled: bool = True):
         self.gpu = gpu_index
+        self.enabled = enabled
         self.proc = None
         self.file = None
 
     def __enter__(self):
+        if not self.enabled:
+            return self
         try:
             self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
@@ -363,7 +366,8 @@ def run_ours(args, rank: int, world: int, device: torch.device):
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
     step_ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
-    with ClockSampler(device.index) as clocks:
+    # only rank 0's samples reach the JSON line; the other ranks run no sampler
+    with ClockSampler(device.index, enabled=rank == 0) as clocks:
         t_start.record()
         h0 = time.perf_counter()
         for i in range(args.steps):
