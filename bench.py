@@ -281,7 +281,8 @@ def run_ours(args, rank: int, world: int, device: torch.device):
                 "out1": torch.empty(n, FEAT, device=device)}
     else:
         # rows dealt to ranks by cost (or contiguous ranges), renumbered into the padded
-        # chunk-major exchange layout; sums are unchanged, only column ids are rewritten
+        # exchange layout (rank-major for the pushes); sums are unchanged, only column ids
+        # are rewritten
         rank_major = args.exchange in ("push", "halo") and args.padded_order == "rank"
         layout = partition.make_padded_layout(rp_cpu, world, args.chunks, balanced=args.layout == "balanced",
                                               row_cost=partition.ROW_COST_IN_ENTRIES, rank_major=rank_major)
