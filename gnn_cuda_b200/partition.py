@@ -8,15 +8,17 @@ unbalanced) — keeps the full feature matrix, and after
 every layer except the last the ranks exchange their output rows so everyone
 again holds the full [N, F] input of the next layer.
 
-Three exchanges are provided, all bit-identical to the one-GPU forward.
-`gcn_forward_push` (the benchmarked path) cuts each rank's rows into pieces,
-writes each piece's output straight into the rank's slice of the next layer's
-input and pushes it to every peer's copy with copy-engine transfers over
-CUDA IPC mappings while the next piece is computed; one small NCCL all_reduce
-per layer boundary serves as the barrier. `gcn_forward_allgather` renumbers
-rows into a padded chunk-major layout and exchanges each piece with an
-asynchronous NCCL all_gather. `gcn_forward_partitioned` keeps global row ids
-and broadcasts each owner's row range.
+Three exchanges are provided, all bit-identical to the one-GPU forward at a
+fixed long-row threshold. `gcn_forward_push` (the benchmarked path) writes each
+layer's output rows straight into the rank's rows of an IPC-mapped copy of the
+next layer's input and sends every peer exactly the rows its CSR reads (the
+halo): stored by the transform's own epilogue (`push_masks`), by a push kernel
+after it, or by copy engines, with one small NCCL all_reduce per layer
+boundary as the barrier; its steps can be captured and replayed as CUDA graphs
+(`PushForwardGraphs`). `gcn_forward_allgather` renumbers rows into a padded
+chunk-major layout and exchanges each piece with an asynchronous NCCL
+all_gather. `gcn_forward_partitioned` keeps global row ids and broadcasts each
+owner's row range.
 """
 from __future__ import annotations
 
